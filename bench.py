@@ -1,0 +1,480 @@
+"""Benchmark of the decode hot path (BASELINE.json metric) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl graft|reference]
+
+Headline workload: one "step" is one batch-1 decode pass over
+the four int4 group-64 GEMV shapes 14336x4096, 4096x14336, 6144x4096 and
+128256x4096 (lm_head), fp16 x -> fp16 y with fp32 accumulation, through the
+C-ABI entry point graft_gemv_int4_sb_f16out.  Weights rotate over 8 seeded
+copies (3.0 GB in all, far beyond the 126 MB L2), so no step finds its weights
+in cache.  `value` is algorithmic bytes (weights + scales/biases + x + y, each
+once) per second over exactly K steps, timed with CUDA events around CUDA-graph
+replays.  Detail entries time the VQ GEMV (config 2), the fused MoE block
+(config 3, us/token), the row-sharded lm_head (config 4) and the read-only
+bandwidth ceiling the same way.
+
+Under torchrun (N > 1) each rank holds its own shard: a row block of an N-times
+taller matrix set (weak scaling), and the fp16 outputs of every GEMV are
+all-gathered to every rank each step; `value` is all ranks' bytes over the
+slowest rank's time.
+
+--impl reference times the reference's own CPU implementation of the path
+(cpuRef, int4-gemv/src/main.mm:64-92, compiled from the reference sources into
+oracle/_ref) on a bounded row sample of the same workload, on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SWEEP = [(14336, 4096), (4096, 14336), (6144, 4096), (128256, 4096)]
+GROUP = 64
+NCOPY = 8
+METRIC = "int4/VQ GEMV HBM GB/s (% of peak) & MoE-block µs/token at 1/2/4/8 B200"
+
+
+def sweep_bytes(shapes) -> int:
+    """Algorithmic bytes of one batch-1 call each: W + S + B + x + y(fp16)."""
+    return sum(M * K // 2 + 2 * 2 * M * (K // GROUP) + 2 * K + 2 * M for M, K in shapes)
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per launch of the int4 GEMV from the committed ncu summary."""
+    p = ROOT / "profiles" / "int4_gemv_sweep.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+# ----------------------------------------------------------------- clocks --
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled while the timed region runs."""
+    Q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.proc = None
+        if uuid is None:
+            return
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", uuid, f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = max(mx, float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------ GPU timing --
+class Timer:
+    """Captures `body(step)` for a chunk of steps into CUDA graphs and replays
+    them; times exactly `steps` steps with CUDA events on the capture stream."""
+
+    def __init__(self, torch, body, chunk: int):
+        self.torch, self.body, self.chunk = torch, body, chunk
+        self.stream = torch.cuda.Stream()
+        self.graphs = {}
+
+    def _graph(self, n: int, start: int):
+        key = (n, start % NCOPY)
+        if key not in self.graphs:
+            torch = self.torch
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(self.stream):
+                self.body(start)            # outside capture: first-call set-up
+                torch.cuda.synchronize()
+                with torch.cuda.graph(g, stream=self.stream):
+                    for i in range(n):
+                        self.body(start + i)
+            self.graphs[key] = g
+        return self.graphs[key]
+
+    def run(self, steps: int) -> None:
+        done = 0
+        while done < steps:
+            n = min(self.chunk, steps - done)
+            n = n if n == self.chunk else n
+            self._graph(n, done).replay()
+            done += n
+
+    def time(self, steps: int, barrier=None) -> float:
+        """Seconds for exactly `steps` steps (device time)."""
+        torch = self.torch
+        # build every graph the timed region replays before timing starts
+        done = 0
+        while done < steps:
+            n = min(self.chunk, steps - done)
+            self._graph(n, done)
+            done += n
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        with torch.cuda.stream(self.stream):
+            self.run(steps)
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        return e0.elapsed_time(e1) / 1e3
+
+
+# --------------------------------------------------------------- workloads --
+def build_sweep(torch, kb, synth, shapes, seed_base: int):
+    sets = []
+    for c in range(NCOPY):
+        per = []
+        for si, (M, K) in enumerate(shapes):
+            w = synth.int4_weights(M, K, GROUP, seed=seed_base + 1000 * c + si)
+            per.append((w["W"], w["SB"]))
+        sets.append(per)
+    xs = [synth.activations(K, seed=seed_base + si) for si, (_, K) in enumerate(shapes)]
+    ys = [torch.empty(M, dtype=torch.float16, device="cuda") for M, _ in shapes]
+    Ps = [kb.gemv_params(M, K, GROUP) for M, K in shapes]
+    return sets, xs, ys, Ps
+
+
+def run_reference_arm(args) -> None:
+    """The reference's own CPU cpuRef on a row sample of each sweep shape."""
+    import numpy as np
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+    L = oracle.ref_lib()
+    if L is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "reference CPU routines (oracle/_ref/libref.so) were not built"}))
+        return
+    rng = np.random.default_rng(0)
+    stride = 1024                    # every 1024th row of each shape: a bounded sample
+    data = []
+    for M, K in SWEEP:
+        m = (M + stride - 1) // stride
+        W = rng.integers(0, 2**32, size=(m, K // 8), dtype=np.uint64).astype(np.uint32)
+        S = np.abs(rng.normal(0, 0.02, (m, K // GROUP))).astype(np.float16)
+        B = (S.astype(np.float32) * -8).astype(np.float16)
+        x = rng.normal(0, 1, K).astype(np.float16)
+        data.append((W, S, B, x, np.empty(m, np.float32), m, K))
+    bytes_step = sweep_bytes([(d[5], d[6]) for d in data])
+
+    def step():
+        for W, S, B, x, y, m, K in data:
+            L.ref_int4_cpuRef(W.ctypes.data, S.ctypes.data, B.ctypes.data, x.ctypes.data,
+                              y.ctypes.data, m, K, GROUP)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    cores = os.cpu_count() or 1
+    v = bytes_step * args.steps / dt / 1e9
+    print(json.dumps({
+        "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "config1_int4_sweep_rowsample", "row_sample": f"1/{stride}",
+                   "shapes": [f"{M}x{K}" for M, K in SWEEP], "group": GROUP},
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores,
+                         "kind": "reference",
+                         "sample": f"every {stride}th row of each config-1 shape per step; "
+                                   "cpuRef (fp64, std::thread x hardware_concurrency)"},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+def cpu_baseline_leg() -> dict:
+    """Reference cpuRef on a bounded sample, rank 0 at N=1 (about 10-20 s)."""
+    import numpy as np
+    import oracle
+    L = oracle.ref_lib()
+    rng = np.random.default_rng(1)
+    M, K = 128256 // 16, 4096                     # 1/16 of the lm_head rows
+    W = rng.integers(0, 2**32, size=(M, K // 8), dtype=np.uint64).astype(np.uint32)
+    S = np.abs(rng.normal(0, 0.02, (M, K // GROUP))).astype(np.float16)
+    B = (S.astype(np.float32) * -8).astype(np.float16)
+    x = rng.normal(0, 1, K).astype(np.float16)
+    nbytes = sweep_bytes([(M, K)])
+    if L is not None:
+        y = np.empty(M, np.float32)
+        f = lambda: L.ref_int4_cpuRef(W.ctypes.data, S.ctypes.data, B.ctypes.data,  # noqa
+                                      x.ctypes.data, y.ctypes.data, M, K, GROUP)
+        kind, desc = "reference", "cpuRef (fp64, all host threads)"
+    else:
+        SB = np.stack([S, B], -1)
+        f = lambda: oracle.gemv_int4_sb(W, SB, x, GROUP)  # noqa
+        kind, desc = "port", "oracle restatement (fp64, all host threads)"
+    f()
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 8.0 and reps < 200:
+        f()
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count() or 1,
+            "kind": kind, "sample": f"{M}x{K} rows (1/16 of lm_head), {reps} calls; {desc}"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30000)
+    ap.add_argument("--warmup", type=int, default=3000)
+    ap.add_argument("--impl", default="graft", choices=["graft", "reference"])
+    ap.add_argument("--no-detail", action="store_true", help="headline only")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import kernels_b200 as kb
+    from kernels_b200 import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    kb.load()
+    peaks = measured_peaks()
+    # each rank holds a row block of its own copy of every shape (weak scaling)
+    sets, xs, ys, Ps = build_sweep(torch, kb, synth, SWEEP, seed_base=7919 * rank)
+    bytes_step = sweep_bytes(SWEEP)
+    gathered = None
+    if world > 1:
+        gathered = [torch.empty(world * M, dtype=torch.float16, device="cuda") for M, _ in SWEEP]
+
+    def step(i):
+        c = sets[i % NCOPY]
+        for (W, SB), x, y, P in zip(c, xs, ys, Ps):
+            kb.gemv_int4_sb_f16out(W, SB, x, y, P)
+        if gathered is not None:
+            for y, g in zip(ys, gathered):
+                dist.all_gather_into_tensor(g, y)
+
+    chunk = 200
+    timer = Timer(torch, step, chunk)
+    timer.run(args.warmup)
+    torch.cuda.synchronize()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid)
+    time.sleep(0.3)
+    dt = timer.time(args.steps, barrier)
+    clocks = sampler.stop()
+    if dist is not None:
+        t = torch.tensor([dt], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    value = world * bytes_step * args.steps / dt / 1e9
+    gpu_launches = len(SWEEP) * args.steps
+
+    # roofline of the dominant kernel: the same launches, achieved = bytes / time
+    achieved = bytes_step * args.steps / dt / 1e9
+    traffic = profile_traffic()
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": traffic, "peak_source": peaks["source"],
+                "kernel": "int4_gemv_kernel (graft_gemv_int4_sb_f16out)",
+                "bytes_per_launch": bytes_step // len(SWEEP)}
+
+    detail = {}
+    e2e = None
+    if rank == 0 or world == 1:
+        e2e = measure_e2e(torch, kb, sets, xs, Ps, steps=min(args.steps, 3000))
+    if not args.no_detail and world == 1:
+        detail = measure_detail(torch, kb, synth, timer_cls=Timer)
+        detail["sweep_per_shape"] = measure_per_shape(torch, kb, sets, xs, ys, Ps)
+        roofline["frac_of_read_ceiling"] = round(
+            achieved / detail["stream_read_ceiling_gbs"], 4)
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        cpu = cpu_baseline_leg()
+
+    del timer
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4xf16->f32acc->f16",
+            "data": "synthetic (seeded, BASELINE config 1 distributions)",
+            "config": {"workload": "config1_int4_sweep_batch1",
+                       "shapes": [f"{M}x{K}" for M, K in SWEEP], "group": GROUP,
+                       "bytes_per_step": bytes_step, "l2": f"inputs larger than L2: {NCOPY} "
+                       "rotating weight copies (3.0 GB) per rank",
+                       "parallelism": f"rowshard{world}" if world > 1 else "single",
+                       "timing": f"CUDA events around CUDA-graph replays ({chunk} steps/graph)"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+            "gpu_launches": gpu_launches, "detail": detail,
+        }
+        print(json.dumps(out))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def measure_e2e(torch, kb, sets, xs, Ps, steps: int) -> dict:
+    """Same metric through the C-ABI with host buffers: per step, x of every
+    shape is copied in from pinned host memory and every y is read back."""
+    hx = [x.cpu().pin_memory() for x in xs]
+    hy = [torch.empty(P.M, dtype=torch.float16).pin_memory() for P in Ps]
+    dx = [torch.empty_like(x) for x in xs]
+    dy = [torch.empty(P.M, dtype=torch.float16, device="cuda") for P in Ps]
+
+    def body(i):
+        c = sets[i % NCOPY]
+        for h, d in zip(hx, dx):
+            d.copy_(h, non_blocking=True)
+        for (W, SB), x, y, P in zip(c, dx, dy, Ps):
+            kb.gemv_int4_sb_f16out(W, SB, x, y, P)
+        for d, h in zip(dy, hy):
+            h.copy_(d, non_blocking=True)
+
+    t = Timer(torch, body, 100)
+    t.run(100)
+    dt = t.time(steps)
+    nbytes = sweep_bytes(SWEEP)
+    return {"value": round(nbytes * steps / dt / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs),
+            "d2h_bytes_per_step": sum(P.M * 2 for P in Ps),
+            "ms_per_step": round(dt / steps * 1e3, 5)}
+
+
+def measure_per_shape(torch, kb, sets, xs, ys, Ps) -> dict:
+    res = {}
+    for si, P in enumerate(Ps):
+        def body(i, si=si):
+            W, SB = sets[i % NCOPY][si]
+            kb.gemv_int4_sb_f16out(W, SB, xs[si], ys[si], P)
+        t = Timer(torch, body, 400)
+        t.run(400)
+        steps = 4000
+        dt = t.time(steps)
+        nb = sweep_bytes([(P.M, P.K)])
+        res[f"{P.M}x{P.K}"] = {"us": round(dt / steps * 1e6, 3),
+                               "gbs": round(nb * steps / dt / 1e9, 1)}
+    return res
+
+
+def measure_detail(torch, kb, synth, timer_cls) -> dict:
+    d = {}
+    # read-only ceiling over the same kind of rotation (8 x 1 GB)
+    bufs = [torch.empty(1 << 30, dtype=torch.uint8, device="cuda") for _ in range(4)]
+    sink = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t = timer_cls(torch, lambda i: kb.stream_read(bufs[i % 4], sink, (1 << 30) // 16), 20)
+    t.run(20)
+    dt = t.time(200)
+    d["stream_read_ceiling_gbs"] = round((1 << 30) * 200 / dt / 1e9, 1)
+    del bufs
+
+    # VQ config 2 (per-row scale, fp16 y)
+    vq = {}
+    for M, K in [(4096, 4096), (14336, 4096)]:
+        ws = [synth.vq_weights(M, K, seed=c) for c in range(NCOPY)]
+        x = synth.activations(K, seed=5)
+        y = torch.empty(M, dtype=torch.float16, device="cuda")
+        P = kb.vq_params(M, K)
+        t = timer_cls(torch, lambda i: kb.gemv_vq_ex(ws[i % NCOPY]["IDX"], ws[i % NCOPY]["C"],
+                                                     ws[i % NCOPY]["S"], K, x, y, P), 400)
+        t.run(400)
+        steps = 4000
+        dt = t.time(steps)
+        nb = M * K // 2 + 2 * M + 1024 + 2 * K + 2 * M
+        vq[f"{M}x{K}"] = {"us": round(dt / steps * 1e6, 3), "gbs": round(nb * steps / dt / 1e9, 1)}
+        del ws
+    d["vq_config2"] = vq
+
+    # MoE config 3 (gpt-oss-120b shape, 128 experts, top-4, BASELINE format)
+    P = kb.moe_params(2880, 2880, 128, 4)
+    pool, R = synth.moe_pool(P, scale_f16=True, has_bias_out=False, act_f16=True, seed=0)
+    xs_ = [synth.activations(2880, seed=s) for s in range(16)]
+    y = torch.empty(2880, dtype=torch.float16, device="cuda")
+    ws = kb.MoEWorkspace(P)
+    fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=True,
+                        n_experts=128)
+    t = timer_cls(torch, lambda i: kb.moe_block_ex(pool, R, xs_[i % 16], y, P, fmt, ws), 200)
+    t.run(200)
+    steps = 2000
+    dt = t.time(steps)
+    nb = 56782080
+    d["moe_config3"] = {"us_per_token": round(dt / steps * 1e6, 3),
+                        "gbs": round(nb * steps / dt / 1e9, 1),
+                        "lower_bound_us_at_peak": round(nb / (measured_peaks()["hbm_gbs"] * 1e3), 3),
+                        "launches_per_token": 3,
+                        "note": "16 rotating tokens; the experts they select (512 MB pool "
+                                "reads) mostly miss L2"}
+    return d
+
+
+if __name__ == "__main__":
+    main()

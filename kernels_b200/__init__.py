@@ -1,0 +1,173 @@
+"""kernels_b200 -- B200 (sm_100a) decode hot path of agastya-choudhary123/kernels.
+
+Host-side mirror of the reference's kernel interface over libcuda-graft.so:
+each function below has the name of the Metal kernel it replaces and takes its
+buffers in the kernel's [[buffer(i)]] order (params struct included), e.g.
+
+    P = gemv_params(M, K, G)                        # GemvParams
+    xsum32(x, xs, P)                                # int4-gemv/src/kernels.metal:54
+    gemv_int4_wide_unroll(W, SB, None, x, y, xs, P) # int4-gemv/src/kernels.metal:399
+
+Buffers are device tensors (anything with .data_ptr()) or raw device
+addresses (int).  Work is enqueued on the current torch CUDA stream unless a
+stream handle is given.  A non-zero library status raises GraftError.  There is
+no CPU fallback: if the library is missing, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from ._lib import (GemvParams, GraftError, MoEFormat, MoEParams, MoEScratch, VQParams, call,
+                   load)
+
+__all__ = [
+    "GemvParams", "VQParams", "MoEParams", "MoEFormat", "MoEScratch", "GraftError",
+    "load", "version", "gemv_params", "xsum32", "gemv_int4_wide_unroll", "gemv_int4_fused",
+    "gemv_int4_simd", "gemv_int4_sb_f16out", "stream_read", "vq_params", "gemv_vq_wide",
+    "gemv_vq_ex", "vq_decode", "moe_params", "moe_router_topk", "moe_fused_gate_up_swiglu",
+    "moe_fused_down_combine", "moe_fused_gate_up_swiglu_at", "moe_fused_down_combine_at",
+    "MoEWorkspace", "moe_block", "moe_block_ex", "moe_format",
+]
+
+
+def _p(t) -> int | None:
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _s(stream) -> int | None:
+    if stream is not None:
+        return stream if isinstance(stream, int) else stream.cuda_stream
+    import torch
+    return torch.cuda.current_stream().cuda_stream
+
+
+def version() -> str:
+    return load().graft_version().decode()
+
+
+# ------------------------------------------------------------------- int4 --
+def gemv_params(M: int, K: int, G: int) -> GemvParams:
+    P = GemvParams()
+    call("graft_gemv_params", M, K, G, C.byref(P))
+    return P
+
+
+def xsum32(x, xs, P: GemvParams, stream=None) -> None:
+    call("graft_xsum32", _p(x), _p(xs), C.byref(P), _s(stream))
+
+
+def gemv_int4_wide_unroll(W, SB, unused, x, y, xs, P: GemvParams, stream=None) -> None:
+    call("graft_gemv_int4_wide_unroll", _p(W), _p(SB), _p(unused), _p(x), _p(y), _p(xs),
+         C.byref(P), _s(stream))
+
+
+gemv_int4_fused = gemv_int4_wide_unroll   # v4 computes the same y from the same buffers
+
+
+def gemv_int4_simd(W, S, B, x, y, xs, P: GemvParams, stream=None) -> None:
+    call("graft_gemv_int4_simd", _p(W), _p(S), _p(B), _p(x), _p(y), _p(xs), C.byref(P),
+         _s(stream))
+
+
+def gemv_int4_sb_f16out(W, SB, x, y, P: GemvParams, stream=None) -> None:
+    call("graft_gemv_int4_sb_f16out", _p(W), _p(SB), _p(x), _p(y), C.byref(P), _s(stream))
+
+
+def stream_read(src, sink, nquads: int, stream=None) -> None:
+    call("graft_stream_read", _p(src), _p(sink), nquads, _s(stream))
+
+
+# --------------------------------------------------------------------- VQ --
+def vq_params(M: int, K: int, cb_size: int = 256) -> VQParams:
+    return VQParams(M, K, K // 32, cb_size)
+
+
+def gemv_vq_wide(IDX, Cb, S, x, y, P: VQParams, stream=None) -> None:
+    call("graft_gemv_vq_wide", _p(IDX), _p(Cb), _p(S), _p(x), _p(y), C.byref(P), _s(stream))
+
+
+def gemv_vq_ex(IDX, Cb, S, scale_group: int, x, y, P: VQParams, stream=None) -> None:
+    import torch
+    y_f16 = int(getattr(y, "dtype", None) == torch.float16)
+    call("graft_gemv_vq_ex", _p(IDX), _p(Cb), _p(S), scale_group, _p(x), _p(y), y_f16,
+         C.byref(P), _s(stream))
+
+
+def vq_decode(IDX, Cb, out, n_idx: int, stream=None) -> None:
+    call("graft_vq_decode", _p(IDX), _p(Cb), _p(out), n_idx, _s(stream))
+
+
+# -------------------------------------------------------------------- MoE --
+def moe_params(hidden: int, inter: int, n_experts: int, top_k: int) -> MoEParams:
+    P = MoEParams()
+    call("graft_moe_params", hidden, inter, n_experts, top_k, C.byref(P))
+    return P
+
+
+def moe_format(scale_f16=False, has_bias_out=True, act_f16=False, y_f16=False,
+               expert_lo=0, expert_hi=None, n_experts=None) -> MoEFormat:
+    hi = expert_hi if expert_hi is not None else (n_experts if n_experts is not None else 256)
+    return MoEFormat(int(scale_f16), int(has_bias_out), int(act_f16), int(y_f16),
+                     expert_lo, hi)
+
+
+def moe_router_topk(R, x, idx, wgt, P: MoEParams, xsh, xh, stream=None) -> None:
+    call("graft_moe_router_topk", _p(R), _p(x), _p(idx), _p(wgt), C.byref(P), _p(xsh), _p(xh),
+         _s(stream))
+
+
+def moe_fused_gate_up_swiglu(pool, idx, xh, h, P: MoEParams, stream=None) -> None:
+    call("graft_moe_fused_gate_up_swiglu", _p(pool), _p(idx), _p(xh), _p(h), C.byref(P),
+         _s(stream))
+
+
+def moe_fused_down_combine(pool, idx, wgt, h, y, P: MoEParams, stream=None) -> None:
+    call("graft_moe_fused_down_combine", _p(pool), _p(idx), _p(wgt), _p(h), _p(y), C.byref(P),
+         _s(stream))
+
+
+def moe_fused_gate_up_swiglu_at(pool, idx, xh, h, P: MoEParams, xsh, stream=None) -> None:
+    call("graft_moe_fused_gate_up_swiglu_at", _p(pool), _p(idx), _p(xh), _p(h), C.byref(P),
+         _p(xsh), _s(stream))
+
+
+def moe_fused_down_combine_at(pool, idx, wgt, h, y, P: MoEParams, xsh, stream=None) -> None:
+    call("graft_moe_fused_down_combine_at", _p(pool), _p(idx), _p(wgt), _p(h), _p(y),
+         C.byref(P), _p(xsh), _s(stream))
+
+
+class MoEWorkspace:
+    """One device buffer carved into the scratch the three MoE kernels share
+    (selected experts, weights, resident-expert list, fp16 x, h, sum(h))."""
+
+    def __init__(self, P: MoEParams, device=None):
+        import torch
+        n = load().graft_moe_scratch_bytes(C.byref(P))
+        self.buffer = torch.empty(n + 256, dtype=torch.uint8, device=device or "cuda")
+        base = (self.buffer.data_ptr() + 255) & ~255
+        self.scratch = MoEScratch()
+        call("graft_moe_scratch_carve", base, n, C.byref(P), C.byref(self.scratch))
+        self.P = P
+
+    def tensor(self, name: str, dtype, numel: int):
+        """A view of one scratch field (idx, wgt, local, xh, h, xsh) as a tensor."""
+        import torch
+        addr = getattr(self.scratch, name)
+        off = addr - self.buffer.data_ptr()
+        nbytes = numel * torch.empty((), dtype=dtype).element_size()
+        return self.buffer[off:off + nbytes].view(dtype)
+
+
+def moe_block(pool, R, x, y, P: MoEParams, ws: MoEWorkspace, stream=None) -> None:
+    call("graft_moe_block", _p(pool), _p(R), _p(x), _p(y), C.byref(P), C.byref(ws.scratch),
+         _s(stream))
+
+
+def moe_block_ex(pool, R, x, y, P: MoEParams, fmt: MoEFormat | None, ws: MoEWorkspace,
+                 stream=None) -> None:
+    call("graft_moe_block_ex", _p(pool), _p(R), _p(x), _p(y), C.byref(P),
+         C.byref(fmt) if fmt is not None else None, C.byref(ws.scratch), _s(stream))

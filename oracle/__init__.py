@@ -1,0 +1,200 @@
+"""TEST INFRASTRUCTURE ONLY -- numpy binding of the CPU oracle.
+
+liboracle.so (oracle.cpp, cpu_fast.cpp) restates the reference's fp64 CPU
+references; _ref/libref.so (when built) runs the reference's own routines.
+Only tests/, __graft_entry__.smoke() and the CPU-baseline leg of bench.py use
+this package; the product (libcuda-graft.so, kernels_b200) never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "liboracle.so"
+REF_LIB = HERE / "_ref" / "libref.so"
+
+_P = C.c_void_p
+_U32, _U64, _INT = C.c_uint32, C.c_uint64, C.c_int
+
+
+def build(ref: bool = True) -> None:
+    """Compiles liboracle.so, and _ref/libref.so when the reference checkout exists."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    if ref:
+        subprocess.run([str(HERE / "ref_build.sh")], check=True, capture_output=True)
+
+
+_lib = None
+_ref = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            build(ref=False)
+        L = C.CDLL(str(LIB))
+        L.oracle_gemv_int4_sep.argtypes = [_P, _P, _P, _P, _P, _U32, _U32, _U32, _INT]
+        L.oracle_gemv_int4_sb.argtypes = [_P, _P, _P, _P, _U32, _U32, _U32, _INT]
+        L.oracle_xsum32.argtypes = [_P, _P, _U32]
+        L.oracle_gemv_vq.argtypes = [_P, _P, _P, _U32, _P, _P, _U32, _U32, _INT]
+        L.oracle_vq_decode.argtypes = [_P, _P, _P, _U64]
+        L.oracle_moe_block.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _INT]
+        L.oracle_moe_block.restype = _INT
+        L.cpu_fast_gemv_int4_sb.argtypes = [_P, _P, _P, _P, _U32, _U32, _U32, _INT]
+        L.cpu_fast_gemv_int4_sb.restype = _INT
+        _lib = L
+    return _lib
+
+
+def ref_lib() -> C.CDLL | None:
+    """The reference's own CPU routines, or None if they were not built here."""
+    global _ref
+    if _ref is None and REF_LIB.exists():
+        L = C.CDLL(str(REF_LIB))
+        L.ref_int4_cpuRef.argtypes = [_P, _P, _P, _P, _P, _U32, _U32, _U32]
+        L.ref_int4_cpuRefRows.argtypes = [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32]
+        L.ref_int4_sb.argtypes = [_P, _P, _P, _P, _U32, _U32, _U32]
+        L.ref_vq_gemv.argtypes = [_P, _P, _P, _P, _P, _U32, _U32]
+        L.ref_moe_block.argtypes = [_P, _P, _P, _U32, _U32, _U32, _U32] + [_U64] * 8 + \
+            [_P, _P, _P, _P]
+        _ref = L
+    return _ref
+
+
+def _ptr(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def _u16(a: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(a).view(np.uint16)
+
+
+# ------------------------------------------------------------ restatement --
+def gemv_int4_sep(W, S, B, x, G: int, nthreads: int = 0) -> np.ndarray:
+    """fp64 y of the separate-S/B int4 GEMV (int4-gemv/src/main.mm:64-79)."""
+    M, K = W.shape[0], W.shape[1] * 8
+    y = np.empty(M, np.float64)
+    lib().oracle_gemv_int4_sep(_ptr(np.ascontiguousarray(W)), _ptr(_u16(S)), _ptr(_u16(B)),
+                               _ptr(_u16(x)), _ptr(y), M, K, G, nthreads)
+    return y
+
+
+def gemv_int4_sb(W, SB, x, G: int, nthreads: int = 0) -> np.ndarray:
+    """fp64 y of the interleaved-SB int4 GEMV (vq-gemv/src/main.mm:66-80)."""
+    M, K = W.shape[0], W.shape[1] * 8
+    y = np.empty(M, np.float64)
+    lib().oracle_gemv_int4_sb(_ptr(np.ascontiguousarray(W)), _ptr(_u16(SB)), _ptr(_u16(x)),
+                              _ptr(y), M, K, G, nthreads)
+    return y
+
+
+def xsum32(x) -> np.ndarray:
+    K = x.shape[0]
+    xs = np.empty(K // 32, np.float32)
+    lib().oracle_xsum32(_ptr(_u16(x)), _ptr(xs), K)
+    return xs
+
+
+def gemv_vq(IDX, Cb, S, scale_group: int, x, nthreads: int = 0) -> np.ndarray:
+    """fp64 y of the VQ GEMV (vq-gemv/src/main.mm:51-65), any scale group."""
+    M, K = IDX.shape[0], IDX.shape[1] * 2
+    y = np.empty(M, np.float64)
+    lib().oracle_gemv_vq(_ptr(np.ascontiguousarray(IDX)), _ptr(_u16(Cb)), _ptr(_u16(S)),
+                         scale_group, _ptr(_u16(x)), _ptr(y), M, K, nthreads)
+    return y
+
+
+def vq_decode(IDX, Cb) -> np.ndarray:
+    IDX = np.ascontiguousarray(IDX).reshape(-1)
+    out = np.empty(IDX.size * 2, np.uint16)
+    lib().oracle_vq_decode(_ptr(IDX), _ptr(_u16(Cb)), _ptr(out), IDX.size)
+    return out
+
+
+class MoECfg(C.Structure):
+    _fields_ = [("hidden", _U32), ("inter", _U32), ("n_experts", _U32), ("top_k", _U32),
+                ("group", _U32), ("scale_bf16", _U32), ("has_bias_out", _U32),
+                ("router_f16", _U32), ("expert_lo", _U32), ("expert_hi", _U32),
+                ("blob", _U64), ("off_gate", _U64), ("off_up", _U64), ("off_down", _U64),
+                ("sub_w", _U64), ("sub_s", _U64), ("sub_b", _U64), ("sub_bi", _U64)]
+
+
+def moe_cfg(P, scale_bf16=True, has_bias_out=True, router_f16=False, expert_lo=0,
+            expert_hi=None) -> MoECfg:
+    """Oracle config from a kernels_b200 MoEParams (same blob layout)."""
+    return MoECfg(P.hidden, P.inter, P.n_experts, P.top_k, 64, int(scale_bf16),
+                  int(has_bias_out), int(router_f16), expert_lo,
+                  P.n_experts if expert_hi is None else expert_hi, P.blob, P.off_gate,
+                  P.off_up, P.off_down, P.sub_w, P.sub_s, P.sub_b, P.sub_bi)
+
+
+def moe_block(cfg: MoECfg, pool: np.ndarray, R: np.ndarray, x: np.ndarray, nthreads: int = 0):
+    """fp64 MoE block (moe-fused/src/main.mm:302-334): idx, wgt, logits, h, y."""
+    T, E, H, I = cfg.top_k, cfg.n_experts, cfg.hidden, cfg.inter
+    idx = np.empty(T, np.uint32)
+    wgt = np.empty(T, np.float64)
+    logits = np.empty(E, np.float64)
+    h = np.empty((T, I), np.float64)
+    y = np.empty(H, np.float64)
+    rc = lib().oracle_moe_block(C.byref(cfg), _ptr(np.ascontiguousarray(pool)),
+                                _ptr(np.ascontiguousarray(R)), _ptr(np.ascontiguousarray(x)),
+                                _ptr(idx), _ptr(wgt), _ptr(logits), _ptr(h), _ptr(y), nthreads)
+    if rc != 0:
+        raise ValueError("oracle_moe_block rejected the configuration")
+    return idx, wgt, logits, h, y
+
+
+def cpu_fast_gemv_int4_sb(W, SB, x, G: int, nthreads: int = 0):
+    """The timed fp32 CPU baseline; returns (y fp32, threads used)."""
+    M, K = W.shape[0], W.shape[1] * 8
+    y = np.empty(M, np.float32)
+    n = lib().cpu_fast_gemv_int4_sb(_ptr(np.ascontiguousarray(W)), _ptr(_u16(SB)),
+                                    _ptr(_u16(x)), _ptr(y), M, K, G, nthreads)
+    return y, n
+
+
+# -------------------------------------------------- the reference, run here --
+def ref_int4_cpuRef(W, S, B, x, G: int) -> np.ndarray:
+    L = ref_lib()
+    M, K = W.shape[0], W.shape[1] * 8
+    y = np.empty(M, np.float32)
+    L.ref_int4_cpuRef(_ptr(np.ascontiguousarray(W)), _ptr(_u16(S)), _ptr(_u16(B)),
+                      _ptr(_u16(x)), _ptr(y), M, K, G)
+    return y
+
+
+def ref_int4_sb(W, SB, x, G: int) -> np.ndarray:
+    L = ref_lib()
+    M, K = W.shape[0], W.shape[1] * 8
+    y = np.empty(M, np.float32)
+    L.ref_int4_sb(_ptr(np.ascontiguousarray(W)), _ptr(_u16(SB)), _ptr(_u16(x)), _ptr(y), M, K, G)
+    return y
+
+
+def ref_vq(IDX, Cb, S, x) -> np.ndarray:
+    L = ref_lib()
+    M, K = IDX.shape[0], IDX.shape[1] * 2
+    y = np.empty(M, np.float32)
+    L.ref_vq_gemv(_ptr(np.ascontiguousarray(IDX)), _ptr(_u16(Cb)), _ptr(_u16(S)),
+                  _ptr(_u16(x)), _ptr(y), M, K)
+    return y
+
+
+def ref_moe_block(P, pool, R, x):
+    L = ref_lib()
+    T, E, H = P.top_k, P.n_experts, P.hidden
+    idx = np.empty(T, np.uint32)
+    wgt = np.empty(T, np.float64)
+    logits = np.empty(E, np.float64)
+    y = np.empty(H, np.float64)
+    L.ref_moe_block(_ptr(np.ascontiguousarray(pool)), _ptr(np.ascontiguousarray(R, np.float32)),
+                    _ptr(np.ascontiguousarray(x, np.float32)), H, P.inter, E, T, P.blob,
+                    P.off_gate, P.off_up, P.off_down, P.sub_w, P.sub_s, P.sub_b, P.sub_bi,
+                    _ptr(idx), _ptr(wgt), _ptr(logits), _ptr(y))
+    return idx, wgt, logits, y

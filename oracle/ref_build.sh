@@ -1,0 +1,43 @@
+#!/usr/bin/env bash
+# ref_build.sh -- build the reference's own CPU reference routines as a checker.
+#
+# Pulls fixed line ranges out of the reference sources (read in place, never
+# copied into the repository) into oracle/_ref/*.inc and compiles
+# oracle/ref_wrap.cpp against them into oracle/_ref/libref.so.  oracle/_ref/ is
+# git-ignored; it travels with the working tree so the reference CPU arm of
+# bench.py can run on a machine that has no reference checkout.
+#
+# Usage: oracle/ref_build.sh [REFERENCE_ROOT]   (default /root/reference)
+# Exits 0 without building when the reference checkout is absent.
+set -euo pipefail
+HERE="$(cd "$(dirname "$0")" && pwd)"
+REF="${1:-/root/reference}"
+OUT="$HERE/_ref"
+if [ ! -d "$REF/int4-gemv/src" ]; then
+    echo "ref_build: no reference checkout at $REF; keeping existing $OUT (if any)"
+    exit 0
+fi
+mkdir -p "$OUT"
+
+# extract FILE RANGES... -> OUT/NAME, then check that an expected line is present
+extract() {
+    local name="$1" file="$2" expect="$3"; shift 3
+    : > "$OUT/$name"
+    for r in "$@"; do
+        printf '#line %s "%s"\n' "${r%%,*}" "$file" >> "$OUT/$name"
+        sed -n "${r}p" "$REF/$file" >> "$OUT/$name"
+    done
+    grep -q -- "$expect" "$OUT/$name" || { echo "ref_build: $file changed (no '$expect')" >&2; exit 1; }
+}
+
+extract int4_ref.inc  int4-gemv/src/main.mm 'static void cpuRef(' 26,26 56,92
+extract vq_ref.inc    vq-gemv/src/main.mm   'static void vqRefRows(' 25,26 31,33 48,90
+extract moe_proj.inc  moe-fused/src/main.mm 'static void refProj(' 43,72
+extract moe_block.inc moe-fused/src/main.mm 'yref\[i\] += rw\[j\]\*yy\[i\]' 303,333
+
+# -ffp-contract=off: the reference is compiled without FMA contraction on its
+# own target, and the oracle restatement is built the same way, so both
+# evaluate the identical sequence of fp64 roundings.
+g++ -std=c++17 -O2 -march=x86-64-v3 -ffp-contract=off -fPIC -shared -D__fp16=_Float16 \
+    -Wno-unused-function -I "$OUT" "$HERE/ref_wrap.cpp" -o "$OUT/libref.so" -lpthread
+echo "ref_build: built $OUT/libref.so"

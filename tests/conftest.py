@@ -1,0 +1,67 @@
+"""Shared test setup.
+
+Markers: `gpu` tests need a B200 (sm_100) and call the CUDA path through the
+C ABI; everything else runs on the CPU.  GPU tests compare the kernels with the
+CPU oracle (oracle/) or with golden vectors produced by the reference's own
+routines (tests/golden/).
+"""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+GOLDEN = ROOT / "tests" / "golden"
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 GPU (sm_100a)")
+
+
+def _has_gpu() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available() and torch.cuda.get_device_capability(0)[0] == 10
+    except Exception:
+        return False
+
+
+def pytest_collection_modifyitems(config, items):
+    if _has_gpu():
+        return
+    skip = pytest.mark.skip(reason="no sm_100 GPU visible")
+    for it in items:
+        if "gpu" in it.keywords:
+            it.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def lib():
+    from kernels_b200 import build
+    build.build()
+    import kernels_b200
+    return kernels_b200.load()
+
+
+def golden(name: str) -> dict:
+    with np.load(GOLDEN / f"{name}.npz") as z:
+        return {k: z[k] for k in z.files}
+
+
+def norm_rel(got, ref) -> float:
+    """max|got - ref| / max|ref| -- the reference's acceptance metric
+    (int4-gemv/src/main.mm:472-476), here held to the BASELINE's 1e-3."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+# BASELINE: max relative error <= 1e-3 for outputs with fp32 accumulation.  The
+# error is taken relative to the largest reference output, as the reference's
+# own check does; per-element relative error is meaningless for outputs that
+# sit near zero.
+TOL = 1e-3

@@ -1,0 +1,167 @@
+"""GPU parity of the fused MoE block (C ABI): exact top-k, softmax weights and
+the block output against the reference's golden output and the fp64 oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import TOL, golden, norm_rel
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    import torch
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def small_golden(kb):
+    g = golden("moe_small")
+    P = kb.MoEParams(*[int(v) for v in g["params"]])
+    return g, P
+
+
+def test_three_kernels_vs_reference_golden(lib):
+    import torch
+    import kernels_b200 as kb
+    g, P = small_golden(kb)
+    pool, R, x = dev(g["pool"]), dev(g["R"]), dev(g["x"])
+    T, H, I = P.top_k, P.hidden, P.inter
+    idx = torch.empty(T, dtype=torch.int32, device="cuda")
+    wgt = torch.empty(T, dtype=torch.float32, device="cuda")
+    xsh = torch.full((T * I // 32,), 5.0, dtype=torch.float32, device="cuda")
+    xh = torch.empty(H, dtype=torch.float16, device="cuda")
+    h = torch.empty(T * I, dtype=torch.float16, device="cuda")
+    y = torch.full((H,), float("nan"), dtype=torch.float32, device="cuda")
+    kb.moe_router_topk(R, x, idx, wgt, P, xsh, xh)
+    assert np.array_equal(host(idx).view(np.uint32), g["idx"])
+    assert np.allclose(host(wgt), g["wgt"], rtol=1e-5, atol=1e-6)
+    assert np.array_equal(host(xsh), np.zeros(T * I // 32, np.float32))
+    assert np.array_equal(host(xh), g["x"].astype(np.float16))
+    kb.moe_fused_gate_up_swiglu(pool, idx, xh, h, P)
+    kb.moe_fused_down_combine(pool, idx, wgt, h, y, P)
+    assert norm_rel(host(y), g["y"]) <= TOL
+
+    # atomic variant: sum(h) per 32-chunk folded in pass 2, read in pass 3
+    y2 = torch.full((H,), float("nan"), dtype=torch.float32, device="cuda")
+    kb.moe_router_topk(R, x, idx, wgt, P, xsh, xh)
+    kb.moe_fused_gate_up_swiglu_at(pool, idx, xh, h, P, xsh)
+    hsum = host(h).astype(np.float64).reshape(T, I // 32, 32).sum(-1).reshape(-1)
+    assert np.allclose(host(xsh), hsum, rtol=1e-3, atol=1e-3)
+    kb.moe_fused_down_combine_at(pool, idx, wgt, h, y2, P, xsh)
+    assert norm_rel(host(y2), g["y"]) <= TOL
+
+
+def test_block_entry_vs_reference_golden(lib):
+    import torch
+    import kernels_b200 as kb
+    g, P = small_golden(kb)
+    ws = kb.MoEWorkspace(P)
+    y = torch.full((P.hidden,), float("nan"), dtype=torch.float32, device="cuda")
+    kb.moe_block(dev(g["pool"]), dev(g["R"]), dev(g["x"]), y, P, ws)
+    assert np.array_equal(host(ws.tensor("idx", torch.int32, P.top_k)).view(np.uint32), g["idx"])
+    assert norm_rel(host(y), g["y"]) <= TOL
+
+
+def baseline_block(kb, n_experts=128, top_k=4, hidden=2880, inter=2880, seed=0):
+    from kernels_b200 import synth
+    P = kb.moe_params(hidden, inter, n_experts, top_k)
+    pool, R = synth.moe_pool(P, scale_f16=True, has_bias_out=False, act_f16=True, seed=seed)
+    x = synth.activations(hidden, seed=seed)
+    return P, pool, R, x
+
+
+def oracle_block(P, pool, R, x, lo=0, hi=None, f16=True, bias=False):
+    cfg = oracle.moe_cfg(P, scale_bf16=not f16, has_bias_out=bias, router_f16=f16,
+                         expert_lo=lo, expert_hi=hi)
+    xr = host(x)
+    return oracle.moe_block(cfg, host(pool), host(R).view(np.uint16) if f16 else host(R),
+                            xr.view(np.uint16) if f16 else xr)
+
+
+def assert_separated(logits, k):
+    s = np.sort(logits)[::-1]
+    assert np.min(-np.diff(s[:k + 1])) > 1e-4, "test data has an unresolvable router tie"
+
+
+@pytest.mark.parametrize("seed", [0, 1])
+def test_baseline_config3_full_size(lib, seed):
+    """gpt-oss-120b-shaped block, BASELINE format (fp16 router/x/scales, no
+    output bias, fp16 y), 128 experts, top-4."""
+    import torch
+    import kernels_b200 as kb
+    P, pool, R, x = baseline_block(kb, seed=seed)
+    ws = kb.MoEWorkspace(P)
+    fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=True,
+                        n_experts=P.n_experts)
+    y = torch.empty(P.hidden, dtype=torch.float16, device="cuda")
+    kb.moe_block_ex(pool, R, x, y, P, fmt, ws)
+    idx, wgt, logits, h, yref = oracle_block(P, pool, R, x)
+    assert_separated(logits, P.top_k)
+    assert np.array_equal(host(ws.tensor("idx", torch.int32, 4)).view(np.uint32), idx)
+    assert np.allclose(host(ws.tensor("wgt", torch.float32, 4)), wgt, rtol=1e-5, atol=1e-6)
+    assert norm_rel(host(y).astype(np.float32), yref) <= TOL
+
+
+def test_expert_parallel_partials_sum_to_block(lib):
+    """EP on one GPU: eight expert ranges, each rank's partial output; their sum
+    is the full block (the all-reduce the multi-GPU path performs)."""
+    import torch
+    import kernels_b200 as kb
+    P, pool, R, x = baseline_block(kb, seed=2)
+    ws = kb.MoEWorkspace(P)
+    total = torch.zeros(P.hidden, dtype=torch.float32, device="cuda")
+    per = P.n_experts // 8
+    for r in range(8):
+        fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=False,
+                            expert_lo=r * per, expert_hi=(r + 1) * per)
+        y = torch.full((P.hidden,), float("nan"), dtype=torch.float32, device="cuda")
+        kb.moe_block_ex(pool, R, x, y, P, fmt, ws)
+        part = oracle_block(P, pool, R, x, lo=r * per, hi=(r + 1) * per)[4]
+        assert norm_rel(host(y), part) <= TOL if np.any(part) else not np.any(host(y))
+        total += y
+    yref = oracle_block(P, pool, R, x)[4]
+    assert norm_rel(host(total), yref) <= TOL
+
+
+@pytest.mark.parametrize("n_experts,top_k", [(40, 1), (64, 2), (256, 8), (128, 4)])
+def test_router_shapes_and_reference_format(lib, n_experts, top_k):
+    import torch
+    import kernels_b200 as kb
+    from kernels_b200 import synth
+    P = kb.moe_params(256, 320, n_experts, top_k)
+    pool, R = synth.moe_pool(P, scale_f16=False, has_bias_out=True, act_f16=False, seed=top_k)
+    R = R * 20.0        # wide logit spread: no near-ties
+    x = torch.randn(P.hidden, device="cuda")
+    ws = kb.MoEWorkspace(P)
+    y = torch.empty(P.hidden, dtype=torch.float32, device="cuda")
+    kb.moe_block(pool, R, x, y, P, ws)
+    idx, wgt, logits, h, yref = oracle_block(P, pool, R, x, f16=False, bias=True)
+    assert_separated(logits, top_k)
+    assert np.array_equal(host(ws.tensor("idx", torch.int32, top_k)).view(np.uint32), idx)
+    assert norm_rel(host(y), yref) <= TOL
+
+
+def test_router_tie_lowest_index(lib):
+    import torch
+    import kernels_b200 as kb
+    P = kb.moe_params(64, 64, 8, 2)
+    R = torch.zeros(8, 64, device="cuda")
+    R[5] = 1.0
+    R[2] = 1.0
+    R[6] = 0.5
+    x = torch.ones(64, device="cuda")
+    idx = torch.empty(2, dtype=torch.int32, device="cuda")
+    wgt = torch.empty(2, dtype=torch.float32, device="cuda")
+    xsh = torch.empty(4, device="cuda")
+    xh = torch.empty(64, dtype=torch.float16, device="cuda")
+    kb.moe_router_topk(R, x, idx, wgt, P, xsh, xh)
+    assert list(host(idx)) == [2, 5]
+    assert np.allclose(host(wgt), [0.5, 0.5])
