@@ -1,5 +1,6 @@
-// q4_rows.cuh -- the int4 group-affine row-dot engine shared by the GEMV and
-// the MoE kernels.
+// q4_rows.cuh -- the register-direct int4 group-affine row-dot engine: loads
+// go straight to registers.  Used where the pipelined engine (q4_pipe.cuh) does
+// not apply: rows longer than 32768 weights, and the MoE passes.
 //
 // The reference computes, per 32-weight chunk c of a row (int4-gemv/src/kernels.metal:20-30),
 //     y += S[g] * sum_{k in c} q_k x_k  +  B[g] * xs[c],   xs[c] = sum_{k in c} x_k
@@ -19,6 +20,7 @@
 
 namespace graft {
 namespace dev {
+namespace simple {
 
 // Scale/bias storage of a weight matrix.
 enum ScaleLayout : int {
@@ -231,5 +233,6 @@ __device__ __forceinline__ void rows_dot_px(const RowSrc (&rows)[R], const bool 
     }
 }
 
+}  // namespace simple
 }  // namespace dev
 }  // namespace graft

@@ -16,6 +16,7 @@
 
 using namespace graft;
 using namespace graft::dev;
+using namespace graft::dev::simple;
 
 namespace {
 

@@ -1,0 +1,96 @@
+"""Runs one hot-path kernel on seeded synthetic data and prints its timing --
+the counterpart of the reference harness binaries' flags (int4gemv --M --K --G
+--iters, vqgemv --M --K, moefused --experts), without the round-robin tables.
+
+    python -m kernels_b200.run int4 --M 128256 --K 4096 [--G 64] [--iters 5] [--copies 2]
+    python -m kernels_b200.run vq --M 14336 --K 4096
+    python -m kernels_b200.run moe [--experts 128] [--top-k 4]
+    python -m kernels_b200.run stream --mbytes 1024
+
+Each iteration is one launch on a rotating weight copy, timed with CUDA events;
+use it for small profiler captures (a few launches, a few GB).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel", choices=["int4", "vq", "moe", "stream"])
+    ap.add_argument("--M", type=int, default=4096)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--G", type=int, default=64)
+    ap.add_argument("--iters", type=int, default=5)
+    ap.add_argument("--copies", type=int, default=2)
+    ap.add_argument("--experts", type=int, default=128)
+    ap.add_argument("--top-k", type=int, default=4)
+    ap.add_argument("--mbytes", type=int, default=1024)
+    ap.add_argument("--f32out", action="store_true")
+    a = ap.parse_args()
+
+    import torch
+    import kernels_b200 as kb
+    from kernels_b200 import synth
+
+    torch.cuda.set_device(0)
+    if a.kernel == "int4":
+        ws = [synth.int4_weights(a.M, a.K, a.G, seed=c) for c in range(a.copies)]
+        x = synth.activations(a.K)
+        P = kb.gemv_params(a.M, a.K, a.G)
+        nbytes = a.M * a.K // 2 + 4 * a.M * (a.K // a.G) + 2 * a.K + (4 if a.f32out else 2) * a.M
+        if a.f32out:
+            y = torch.empty(a.M, dtype=torch.float32, device="cuda")
+            xs = torch.empty(a.K // 32, dtype=torch.float32, device="cuda")
+            kb.xsum32(x, xs, P)
+            f = lambda i: kb.gemv_int4_wide_unroll(ws[i % a.copies]["W"], ws[i % a.copies]["SB"],  # noqa
+                                                   None, x, y, xs, P)
+        else:
+            y = torch.empty(a.M, dtype=torch.float16, device="cuda")
+            f = lambda i: kb.gemv_int4_sb_f16out(ws[i % a.copies]["W"], ws[i % a.copies]["SB"],  # noqa
+                                                 x, y, P)
+    elif a.kernel == "vq":
+        ws = [synth.vq_weights(a.M, a.K, seed=c) for c in range(a.copies)]
+        x = synth.activations(a.K)
+        y = torch.empty(a.M, dtype=torch.float16, device="cuda")
+        P = kb.vq_params(a.M, a.K)
+        nbytes = a.M * a.K // 2 + 2 * a.M + 1024 + 2 * a.K + 2 * a.M
+        f = lambda i: kb.gemv_vq_ex(ws[i % a.copies]["IDX"], ws[i % a.copies]["C"],  # noqa
+                                    ws[i % a.copies]["S"], a.K, x, y, P)
+    elif a.kernel == "moe":
+        P = kb.moe_params(2880, 2880, a.experts, a.top_k)
+        pool, R = synth.moe_pool(P, scale_f16=True, has_bias_out=False, act_f16=True)
+        xs_ = [synth.activations(2880, seed=s) for s in range(8)]
+        y = torch.empty(2880, dtype=torch.float16, device="cuda")
+        wsp = kb.MoEWorkspace(P)
+        fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=True,
+                            n_experts=a.experts)
+        nbytes = a.top_k * 3 * (2880 * 1440 + 2 * 2 * 2880 * 45) + a.experts * 2880 * 2 + 6 * 2880 \
+            + 4 * a.top_k * 2880
+        f = lambda i: kb.moe_block_ex(pool, R, xs_[i % 8], y, P, fmt, wsp)  # noqa
+    else:
+        n = a.mbytes << 20
+        bufs = [torch.empty(n, dtype=torch.uint8, device="cuda") for _ in range(a.copies)]
+        sink = torch.zeros(1, dtype=torch.int32, device="cuda")
+        nbytes = n
+        f = lambda i: kb.stream_read(bufs[i % a.copies], sink, n // 16)  # noqa
+
+    f(0)
+    torch.cuda.synchronize()
+    times = []
+    for i in range(a.iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        f(i + 1)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3)
+    best = min(times)
+    print(json.dumps({"kernel": a.kernel, "M": a.M, "K": a.K, "best_us": round(best, 3),
+                      "gbs": round(nbytes / best / 1e3, 1), "bytes": nbytes,
+                      "times_us": [round(t, 2) for t in times]}))
+
+
+if __name__ == "__main__":
+    main()
