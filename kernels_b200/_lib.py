@@ -80,6 +80,8 @@ SIGNATURES: dict[str, tuple] = {
     "graft_moe_block": (INT, [P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEScratch), P]),
     "graft_moe_block_ex": (INT, [P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEFormat),
                                  C.POINTER(MoEScratch), P]),
+    "graft_moe_block_noalloc": (INT, [P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEFormat),
+                                      P]),
 }
 
 _lib: C.CDLL | None = None
