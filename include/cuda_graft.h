@@ -134,7 +134,8 @@ int graft_vq_decode(const void* IDX, const void* C, void* out, uint64_t n_idx,
 /* ============================================================ MoE block ===
  * One decode token through a gpt-oss-style MoE block: router + top-k + softmax,
  * gate/up + SwiGLU, down + weighted combine, in three kernels.
- * Expert weights live in one pool: expert e's blob starts at pool + e*blob;
+ * Expert weights live in one pool: expert e's blob starts at pool + e*blob
+ * (with an expert range [expert_lo, expert_hi), at pool + (e-expert_lo)*blob);
  * projection p (gate/up/down) at off_p inside it, and inside a projection W
  * (uint32 [rows][K/8]) at sub_w, S and B ([rows][K/64]) at sub_s/sub_b and the
  * per-row output bias BI ([rows]) at sub_bi (moe-fused/src/main.mm:23-25).
@@ -171,8 +172,9 @@ typedef struct {
     uint32_t has_bias_out; /* 1: per-row output bias BI at sub_bi                   */
     uint32_t act_f16;      /* 0: fp32 R and x (reference)  1: fp16 R and x         */
     uint32_t y_f16;        /* 0: fp32 y                    1: fp16 y               */
-    uint32_t expert_lo;    /* experts in [expert_lo, expert_hi) are resident and   */
-    uint32_t expert_hi;    /* contribute to y (expert parallelism); others skipped */
+    uint32_t expert_lo;    /* experts in [expert_lo, expert_hi) are resident (the  */
+    uint32_t expert_hi;    /* pool holds just these, expert_lo first) and contribute
+                              to y (expert parallelism); the others are skipped    */
 } GraftMoEFormat;
 
 /* router_topk, moe-fused/src/kernels.metal:121-163.  Buffers: 0 R (fp32
@@ -229,9 +231,9 @@ int graft_moe_block(const void* pool, const float* R, const float* x, float* y,
                     graft_stream_t stream);
 
 /* The block in any GraftMoEFormat (NULL = the reference format).  With
- * expert_lo/expert_hi a sub-range, y is this rank's partial sum over the
- * selected experts it holds (zero if none); the caller sums partials across
- * ranks (graft_comm_moe_block_ep does this). */
+ * expert_lo/expert_hi a sub-range, `pool` holds only experts expert_lo ..
+ * expert_hi-1 and y is this rank's partial sum over the selected experts it
+ * holds (zero if none); the caller sums partials across ranks. */
 int graft_moe_block_ex(const void* pool, const void* R, const void* x, void* y,
                        const GraftMoEParams* P, const GraftMoEFormat* fmt,
                        const GraftMoEScratch* scratch, graft_stream_t stream);

@@ -13,6 +13,7 @@ import argparse
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -55,8 +56,8 @@ def build(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> 
     LIBDIR.mkdir(exist_ok=True)
     objdir = LIBDIR / "obj"
     objdir.mkdir(exist_ok=True)
-    objs = []
-    for src in sources():
+
+    def compile_one(src: Path) -> tuple[Path, subprocess.CompletedProcess]:
         obj = objdir / (src.stem + ".o")
         cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-I", str(CSRC),
                "-c", str(src), "-o", str(obj)]
@@ -64,7 +65,13 @@ def build(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> 
             cmd += ["-Xptxas", "-v"]
         if verbose:
             print(" ".join(cmd), flush=True)
-        r = subprocess.run(cmd, capture_output=True, text=True)
+        return obj, subprocess.run(cmd, capture_output=True, text=True)
+
+    # translation units compile independently: one nvcc per source, in parallel
+    with ThreadPoolExecutor(max_workers=min(len(sources()), os.cpu_count() or 1)) as ex:
+        results = list(ex.map(compile_one, sources()))
+    objs = []
+    for src, (obj, r) in zip(sources(), results):
         if r.returncode != 0 or ptxas_v:
             sys.stderr.write(r.stdout + r.stderr)
         if r.returncode != 0:

@@ -110,6 +110,28 @@ struct LaneX {
             xsum[t] = (xs_in && c < c1) ? xs_in[c] : e + o;
         }
     }
+
+    // Same, from activations staged in shared memory as swapped pairs.
+    __device__ __forceinline__ void load_smem(const uint4* __restrict__ xs, int c0, int c1,
+                                              int lane) {
+#pragma unroll
+        for (int t = 0; t < TMAX; ++t) {
+            const int c = c0 + lane + 32 * t;
+            float e = 0.f, o = 0.f;
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                x[t][p] = c < c1 ? xs[4 * c + p] : make_uint4(0, 0, 0, 0);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&x[t][p].x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&x[t][p].y));
+                const float2 cc = __half22float2(*reinterpret_cast<const __half2*>(&x[t][p].z));
+                const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&x[t][p].w));
+                e += (a.x + a.y) + (cc.x + cc.y);
+                o += (b.x + b.y) + (d.x + d.y);
+            }
+            off[t] = fmaf(1024.f, e, 64.f * o);
+            xsum[t] = e + o;
+        }
+    }
 };
 
 // Shared-memory slot: W [R][TMAX*32 chunks][16 B] (as the bulk copies land),
@@ -299,6 +321,109 @@ struct Issuer {
         cp_async_mbar_arrive(bar);
     }
 };
+
+// Issues one unit whose R rows have arbitrary sources (w_row[r] = codes of
+// chunk c0 of row r, s_row/b_row = that row's scale/bias arrays); used where
+// the rows of a unit do not sit at one stride (MoE gate/up pairs, gathered
+// experts).  Scales are copied per lane.  Called by all 32 lanes.
+template <int LAYOUT, int TMAX, int R>
+__device__ __forceinline__ void issue_rows(uint32_t slot, uint32_t bar,
+                                           const uint8_t* const (&w_row)[R],
+                                           const uint8_t* const (&s_row)[R],
+                                           const uint8_t* const (&b_row)[R], int nc, int nrows,
+                                           int lane, const LaneK<TMAX>& lk, const uint8_t* s_end,
+                                           const uint8_t* b_end) {
+    using SL = Slot<LAYOUT, TMAX, R>;
+    const uint32_t rowb = (uint32_t)nc * 16;
+    if (lane == 0) mbar_arrive_expect_tx(bar, rowb * (uint32_t)nrows);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        if (lane == r && r < nrows) {
+            fence_proxy_async_smem();
+            bulk_g2s(slot + r * SL::W_ROW, w_row[r], rowb, bar);
+        }
+    }
+    const uint32_t sbase = slot + SL::W_BYTES;
+#pragma unroll
+    for (int t = 0; t < TMAX; ++t) {
+        if (!lk.live[t]) continue;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            if (r >= nrows) continue;
+            const uint32_t d = sbase + (uint32_t)(((t * R + r) * SL::NW) * 128 + lane * 4);
+            if (LAYOUT == kSBHalf2) {
+                cp_async4(d, s_row[r] + 4 * (size_t)lk.gl[t]);
+            } else {
+                const uint8_t* ps = s_row[r] + 2 * (size_t)lk.gl[t];
+                const uint8_t* pb = b_row[r] + 2 * (size_t)lk.gl[t];
+                const uint8_t* ws = (const uint8_t*)((uintptr_t)ps & ~(uintptr_t)3);
+                const uint8_t* wb = (const uint8_t*)((uintptr_t)pb & ~(uintptr_t)3);
+                if (ws + 4 <= s_end) cp_async4(d, ws);
+                else asm volatile("st.shared.u32 [%0], %1;" ::"r"(d),
+                                  "r"((uint32_t)*(const uint16_t*)ps << (((uintptr_t)ps & 2) * 8)));
+                if (wb + 4 <= b_end) cp_async4(d + 128, wb);
+                else asm volatile("st.shared.u32 [%0], %1;" ::"r"(d + 128),
+                                  "r"((uint32_t)*(const uint16_t*)pb << (((uintptr_t)pb & 2) * 8)));
+            }
+        }
+    }
+    cp_async_mbar_arrive(bar);
+}
+
+// acc[r] += row r's share for rows with arbitrary scale arrays s_row/b_row
+// (separate layouts), lane-copied scales.
+template <int LAYOUT, int TMAX, int R>
+__device__ __forceinline__ void compute_rows(const uint8_t* slot, const LaneX<TMAX>& lx,
+                                             const LaneK<TMAX>& lk, int lane,
+                                             const uint8_t* const (&s_row)[R],
+                                             const uint8_t* const (&b_row)[R], float (&acc)[R]) {
+    using SL = Slot<LAYOUT, TMAX, R>;
+    const uint4* wsm = reinterpret_cast<const uint4*>(slot);
+    const uint32_t* sbw = reinterpret_cast<const uint32_t*>(slot + SL::W_BYTES);
+#pragma unroll
+    for (int t = 0; t < TMAX; ++t) {
+        if (!lk.live[t]) continue;
+        const int cl = lane + 32 * t;
+        uint4 wv[R];
+        float ae[R], ao[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            wv[r] = wsm[r * (SL::W_ROW / 16) + cl];
+            ae[r] = 0.f;
+            ao[r] = 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) dot8q(wv[r].x, lx.x[t][0], ae[r], ao[r]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) dot8q(wv[r].y, lx.x[t][1], ae[r], ao[r]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) dot8q(wv[r].z, lx.x[t][2], ae[r], ao[r]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) dot8q(wv[r].w, lx.x[t][3], ae[r], ao[r]);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const float d = fmaf(ao[r], 0.0625f, ae[r]) - lx.off[t];
+            const int wi = ((t * R + r) * SL::NW) * 32 + lane;
+            float2 sb;
+            if (LAYOUT == kSBHalf2) {
+                sb = sb_pair<LAYOUT>(sbw[wi], 0u, 0u, 0u);
+            } else {
+                const uint32_t sh = (uint32_t)(((uintptr_t)(s_row[r] + 2 * (size_t)lk.gl[t]) & 2) * 8);
+                const uint32_t shb = (uint32_t)(((uintptr_t)(b_row[r] + 2 * (size_t)lk.gl[t]) & 2) * 8);
+                sb = sb_pair<LAYOUT>(sbw[wi], sbw[wi + 32], sh, shb);
+            }
+            acc[r] = fmaf(sb.x, d, fmaf(sb.y, lx.xsum[t], acc[r]));
+        }
+    }
+}
+
+// Stages `n` fp16 activations (16-byte aligned, n % 32 == 0) into shared memory
+// as swapped pairs (the layout LaneX holds), for LaneX::load_smem.  All
+// threads of the CTA call it; no barrier inside.
+__device__ __forceinline__ void stage_swapped(const uint4* __restrict__ src, int n,
+                                              uint4* __restrict__ dst) {
+    for (int i = threadIdx.x; i < n / 8; i += blockDim.x) dst[i] = swap_pairs(ld_ro(src + i));
+}
 
 // Reduces v[0..R-1] over the 32 lanes; afterwards lane r (r < R) holds row r's
 // total.  Butterfly reduce-scatter: R-1 + log2(32/R) shuffles instead of 5R.

@@ -112,7 +112,8 @@ def test_baseline_config3_full_size(lib, seed):
 
 def test_expert_parallel_partials_sum_to_block(lib):
     """EP on one GPU: eight expert ranges, each rank's partial output; their sum
-    is the full block (the all-reduce the multi-GPU path performs)."""
+    is the full block (the all-reduce the multi-GPU path performs).  Each rank's
+    pool holds only its own experts (a view starting at expert r*per)."""
     import torch
     import kernels_b200 as kb
     P, pool, R, x = baseline_block(kb, seed=2)
@@ -123,7 +124,8 @@ def test_expert_parallel_partials_sum_to_block(lib):
         fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=False,
                             expert_lo=r * per, expert_hi=(r + 1) * per)
         y = torch.full((P.hidden,), float("nan"), dtype=torch.float32, device="cuda")
-        kb.moe_block_ex(pool, R, x, y, P, fmt, ws)
+        shard = pool[r * per * P.blob:(r + 1) * per * P.blob]
+        kb.moe_block_ex(shard, R, x, y, P, fmt, ws)
         part = oracle_block(P, pool, R, x, lo=r * per, hi=(r + 1) * per)[4]
         assert norm_rel(host(y), part) <= TOL if np.any(part) else not np.any(host(y))
         total += y
