@@ -23,12 +23,6 @@
 namespace graft {
 namespace dev {
 
-enum ScaleLayout : int {
-    kSBHalf2 = 0,  // interleaved fp16 (scale, bias) pairs [rows][groups][2] (v4..v6)
-    kSepF16 = 1,   // separate fp16 S[rows][groups], B[rows][groups]          (v0..v3, BASELINE MoE)
-    kSepBF16 = 2   // separate bf16 S, B                                       (gpt-oss MoE blobs)
-};
-
 // 8 codes of `w` against the swapped activation pairs of one word:
 //   ae += sum_{j even} (1024 + q_j) x_j,   ao += sum_{j odd} (1024 + 16 q_j) x_j
 // Activations are held as (x4,x0) (x5,x1) (x6,x2) (x7,x3), the mirror of the
