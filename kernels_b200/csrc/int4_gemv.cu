@@ -75,7 +75,7 @@ struct GemvArgs {
 constexpr int kHeadBytes = 256;
 template <int WPG>
 __host__ __device__ inline int smem_after_rings(int K, int rows_max, int parts) {
-    return K * 2 + 16 * WPG + (K / (32 * WPG)) * 8 + rows_max * parts * 4;
+    return XWin<WPG>::uint4s(K) * 16 + (K / (32 * WPG) + 8) * 8 + rows_max * parts * 4;
 }
 
 template <int LAYOUT, bool F16OUT, int WPG, int NW>
@@ -90,9 +90,8 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
     uint8_t* scales = codes + NW * kDepth * PG::CODE_BYTES;
     const int sslot = SG::NARR * a.scap;
     uint4* xf = reinterpret_cast<uint4*>(scales + NW * kDepth * sslot);
-    uint4* zero = xf + a.K / 8;
-    float2* gc = reinterpret_cast<float2*>(zero + WPG);
-    float* cells = reinterpret_cast<float*>(gc + a.K / (32 * WPG));
+    float2* gc = reinterpret_cast<float2*>(xf + XWin<WPG>::uint4s(a.K));
+    float* cells = reinterpret_cast<float*>(gc + a.K / (32 * WPG) + 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles = (a.M + kTileRows - 1) / kTileRows;
@@ -108,16 +107,17 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
         for (int i = 0; i < NW * kDepth; ++i) mbar_init(smem_u32(&bars[i]), kTileArrivals);
         fence_mbar_init();
     }
-    if (threadIdx.x < WPG) zero[threadIdx.x] = make_uint4(0, 0, 0, 0);
     __syncthreads();
     pdl_launch_dependents();
 
     // unit u = warp + NW*i is (tile u / parts, part u % parts)
+    const int dtile = NW / a.parts, dpart = NW - dtile * a.parts;
     struct It {
         int tile, part;
-        __device__ void next(int parts) {
-            part += NW;
-            while (part >= parts) { part -= parts; ++tile; }
+        __device__ void next(int parts, int dt, int dp) {
+            tile += dt;
+            part += dp;
+            if (part >= parts) { part -= parts; ++tile; }
         }
     };
     It iss{warp / a.parts, warp % a.parts}, cmp = iss;
@@ -125,12 +125,13 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
     auto scale_of = [&](int i) { return scales + (warp * kDepth + i) * sslot; };
     auto bar_of = [&](int i) { return smem_u32(&bars[warp * kDepth + i]); };
     auto issue = [&](const It& u, int si) {
-        if (lane != 0) return;
+        // warp-uniform values first, then one lane issues
         const uint32_t cd = smem_u32(code_of(si)), sd = smem_u32(scale_of(si)), bar = bar_of(si);
         const int row0 = r0 + kTileRows * u.tile;
         const int c0 = u.part * PG::CHUNKS, nc = min(PG::CHUNKS, nch - c0);
         const int nseg = (nc + 7) / 8, g0 = c0 / WPG;
         uint32_t bytes = (uint32_t)nseg * kTileRows * 128;
+        if (lane != 0) return;
         SpanCopy sc0{nullptr, 0u, 0u}, sc1{nullptr, 0u, 0u};
         if (a.scale_map) {
             bytes += (uint32_t)(SG::NARR * kTileRows * kWindow * SG::ES);
@@ -158,7 +159,7 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
     // kernel on the stream has finished.
     for (int i = 0; i < kDepth && i < mine; ++i) {
         issue(iss, i);
-        iss.next(a.parts);
+        iss.next(a.parts, dtile, dpart);
     }
     pdl_wait();   // x, and the y this grid writes, may belong to the previous kernel
     stage_x<WPG>(a.x, a.K, a.xs_in, xf, gc);
@@ -168,27 +169,25 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
     LaneGeom<WPG> lg;
     lg.init(lane);
     const uint32_t s_lo = (uint32_t)(uintptr_t)a.S, b_lo = (uint32_t)(uintptr_t)a.B;
+    ScaleView sv;
+    sv.so[0] = sv.so[1] = 0;
+    sv.rs[0] = sv.rs[1] = a.scale_map ? (uint32_t)(kWindow * SG::ES) : srow;
     bool live = true;
     int si = 0;
     uint32_t ph = 0;
     for (int i = 0; i < mine; ++i) {
         const int c0 = cmp.part * PG::CHUNKS, nc = min(PG::CHUNKS, nch - c0);
         const int row0 = r0 + kTileRows * cmp.tile;
-        ScaleView sv;
-        if (a.scale_map) {
-            sv.so[0] = sv.so[1] = 0;
-            sv.rs[0] = sv.rs[1] = (uint32_t)(kWindow * SG::ES);
-        } else {
+        if (!a.scale_map) {
             const uint32_t o = (uint32_t)row0 * srow;
             sv.so[0] = ((s_lo + o) & 15) + (uint32_t)(SG::ES * (c0 / WPG));
             sv.so[1] = ((b_lo + o) & 15) + (uint32_t)(SG::ES * (c0 / WPG));
-            sv.rs[0] = sv.rs[1] = srow;
         }
         if (live) live = wait_tile(bar_of(si), ph, &g_int4_err);
         float acc[2] = {0.f, 0.f};
         if (live)
-            tile_dot<LAYOUT, WPG>(code_of(si), scale_of(si), xf + 4 * c0, gc + c0 / WPG, zero,
-                                  nc / WPG, lane, lg, sv, (uint32_t)a.scap, acc);
+            tile_dot<LAYOUT, WPG>(code_of(si), scale_of(si), xf + cmp.part * XWin<WPG>::STRIDE,
+                                  gc + c0 / WPG, nc / WPG, lane, lg, sv, (uint32_t)a.scap, acc);
         const float v0 = quad_sum(acc[0]), v1 = quad_sum(acc[1]);
         if (t == 0) {
             const int lrow = kTileRows * cmp.tile + lg.R;   // CTA-local rows R and R+8
@@ -198,9 +197,9 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
         __syncwarp();
         if (live && i + kDepth < mine) {
             issue(iss, si);
-            iss.next(a.parts);
+            iss.next(a.parts, dtile, dpart);
         }
-        cmp.next(a.parts);
+        cmp.next(a.parts, dtile, dpart);
         if (++si == kDepth) { si = 0; ph ^= 1u; }
     }
     __syncthreads();

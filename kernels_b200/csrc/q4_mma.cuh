@@ -187,11 +187,23 @@ __device__ __forceinline__ float2 scale_pair(const uint8_t* s, const uint8_t* b)
     return make_float2(bf2f(sv), bf2f(bv));
 }
 
+// x in shared memory: per window of 8 groups, the word fragments (32*WPG
+// uint4) followed by WPG zero fragments; a lane reads its step-j fragment at
+// a fixed offset from the window base -- the real one at step j == g, the
+// zeros otherwise -- so no per-step select is needed.
+template <int WPG>
+struct XWin {
+    static constexpr int WORDS = 32 * WPG;         // fragments of one window
+    static constexpr int STRIDE = WORDS + WPG;     // uint4 per window incl. zeros
+    __host__ __device__ static int uint4s(int K) { return (K / (256 * WPG) + 1) * STRIDE; }
+};
+
 // Per-lane constants of the tile engine (fixed for a warp's lifetime).
 template <int WPG>
 struct LaneGeom {
     int R;         // tile row read for MMA row g (and R+8 for row g+8)
     int offs[8];   // byte offset of this lane's words of group j, tile row R
+    int xoff[8];   // uint4 offset of this lane's x fragments for step j
     __device__ __forceinline__ void init(int lane) {
         const int g = lane >> 2, t = lane & 3;
         R = tile_row_of<WPG>(g);
@@ -200,69 +212,76 @@ struct LaneGeom {
         for (int j = 0; j < kWindow; ++j) {
             const int o = 16 * WPG * j + lo;   // byte in the row's 128*WPG
             offs[j] = (o >> 7) * (kTileRows * 128) + R * 128 + ((((o >> 4) & 7) ^ X) << 4) + (o & 15);
+            xoff[j] = g == j ? (4 * j + t) * WPG : XWin<WPG>::WORDS;
         }
     }
 };
 
-// acc[0] += tile row R, acc[1] += tile row R+8 (R = sigma(g)), over the groups
-// 2t, 2t+1 of the unit (g = lane/4, t = lane%4).  slot: the unit's codes; sc:
-// its scale regions; xf: x fragments of the part's words; gc: (off, sum x) of the part's groups; zero: WPG zero
-// fragments; ng (<= 8): groups in the part; sv: where the scales sit; scap:
-// bytes per scale region.
-template <int LAYOUT, int WPG>
-__device__ __forceinline__ void tile_dot(const uint8_t* slot, const uint8_t* sc, const uint4* xf,
-                                         const float2* gc,
-                                         const uint4* zero, int ng, int lane,
-                                         const LaneGeom<WPG>& lg, const ScaleView& sv,
-                                         uint32_t scap, float (&acc)[2]) {
+template <int LAYOUT, int WPG, bool FULL>
+__device__ __forceinline__ void tile_dot_w(const uint8_t* slot, const uint8_t* sc,
+                                           const uint4* xwin, const float2* gc, int ng, int lane,
+                                           const LaneGeom<WPG>& lg, const ScaleView& sv,
+                                           uint32_t scap, float (&acc)[2]) {
     using SG = ScaleGeom<LAYOUT>;
-    const int g = lane >> 2, t = lane & 3;
-    const uint4* xw = xf + t * WPG;
+    const int t = lane & 3;
     // one accumulator pair per word position: 2*WPG independent MMA chains
     float de[WPG][4], dd[WPG][4];
 #pragma unroll
     for (int i = 0; i < WPG; ++i)
 #pragma unroll
         for (int q = 0; q < 4; ++q) de[i][q] = dd[i][q] = 0.f;
-    auto step = [&](int j) {
-        const uint4* xp = g == j ? xw + 4 * WPG * j : zero;
-        uint32_t wa[WPG], wb[WPG];
-        load_words<WPG>(slot + lg.offs[j], wa);
-        load_words<WPG>(slot + lg.offs[j] + 8 * 128, wb);
 #pragma unroll
-        for (int i = 0; i < WPG; ++i) {
-            const uint4 xv = xp[i];
-            uint32_t ae0, ae1, ao0, ao1, be0, be1, bo0, bo1;
-            decode_word(wa[i], ae0, ae1, ao0, ao1);
-            decode_word(wb[i], be0, be1, bo0, bo1);
-            mma_16816(de[i], ae0, be0, ae1, be1, xv.x, xv.y);
-            mma_16816(dd[i], ao0, bo0, ao1, bo1, xv.z, xv.w);
+    for (int j = 0; j < kWindow; ++j) {
+        if (FULL || j < ng) {
+            const uint4* xp = xwin + lg.xoff[j];
+            uint32_t wa[WPG], wb[WPG];
+            load_words<WPG>(slot + lg.offs[j], wa);
+            load_words<WPG>(slot + lg.offs[j] + 8 * 128, wb);
+#pragma unroll
+            for (int i = 0; i < WPG; ++i) {
+                const uint4 xv = xp[i];
+                uint32_t ae0, ae1, ao0, ao1, be0, be1, bo0, bo1;
+                decode_word(wa[i], ae0, ae1, ao0, ao1);
+                decode_word(wb[i], be0, be1, bo0, bo1);
+                mma_16816(de[i], ae0, be0, ae1, be1, xv.x, xv.y);
+                mma_16816(dd[i], ao0, bo0, ao1, bo1, xv.z, xv.w);
+            }
         }
-    };
-    if (ng == kWindow) {
-#pragma unroll
-        for (int j = 0; j < kWindow; ++j) step(j);
-    } else {
-#pragma unroll
-        for (int j = 0; j < kWindow; ++j)
-            if (j < ng) step(j);
     }
     // column 2t+c of the accumulators is group 2t+c; [q]: tile row R + 8*(q>>1)
+    const uint8_t* s0 = sc + sv.so[0] + lg.R * sv.rs[0] + SG::ES * 2 * t;
+    const uint8_t* b0 = sc + scap + sv.so[1] + lg.R * sv.rs[1] + SG::ES * 2 * t;
+    const float4 kk = *reinterpret_cast<const float4*>(gc + 2 * t);   // groups 2t, 2t+1
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         float e = de[0][q], o = dd[0][q];
 #pragma unroll
         for (int i = 1; i < WPG; ++i) { e += de[i][q]; o += dd[i][q]; }
-        const int G = 2 * t + (q & 1), r = q >> 1;
-        if (G < ng) {
-            const float2 k = gc[G];
-            const float d = fmaf(o, 0.0625f, e) - k.x;
-            const int row = lg.R + 8 * r;
-            const float2 sb = scale_pair<LAYOUT>(sc + sv.so[0] + row * sv.rs[0] + SG::ES * G,
-                                                 sc + scap + sv.so[1] + row * sv.rs[1] + SG::ES * G);
-            acc[r] = fmaf(sb.x, d, fmaf(sb.y, k.y, acc[r]));
+        const int c = q & 1, r = q >> 1;
+        if (FULL || 2 * t + c < ng) {
+            const float off = c ? kk.z : kk.x, xsum = c ? kk.w : kk.y;
+            const float d = fmaf(o, 0.0625f, e) - off;
+            const float2 sb = scale_pair<LAYOUT>(s0 + r * 8 * sv.rs[0] + SG::ES * c,
+                                                 b0 + r * 8 * sv.rs[1] + SG::ES * c);
+            acc[r] = fmaf(sb.x, d, fmaf(sb.y, xsum, acc[r]));
         }
     }
+}
+
+// acc[0] += tile row R, acc[1] += tile row R+8 (R = sigma(g)), over the groups
+// 2t, 2t+1 of the unit (g = lane/4, t = lane%4).  slot: the unit's codes; sc:
+// its scale regions; xwin: the part's x window; gc: (off, sum x) of the
+// part's groups (16-byte aligned); ng (<= 8): groups in the part; sv: where
+// the scales sit; scap: bytes per scale region.
+template <int LAYOUT, int WPG>
+__device__ __forceinline__ void tile_dot(const uint8_t* slot, const uint8_t* sc,
+                                         const uint4* xwin, const float2* gc, int ng, int lane,
+                                         const LaneGeom<WPG>& lg, const ScaleView& sv,
+                                         uint32_t scap, float (&acc)[2]) {
+    if (ng == kWindow)
+        tile_dot_w<LAYOUT, WPG, true>(slot, sc, xwin, gc, ng, lane, lg, sv, scap, acc);
+    else
+        tile_dot_w<LAYOUT, WPG, false>(slot, sc, xwin, gc, ng, lane, lg, sv, scap, acc);
 }
 
 // Sum over the 4 lanes t of a row quad; every lane ends with the total.
@@ -272,14 +291,21 @@ __device__ __forceinline__ float quad_sum(float v) {
     return v;
 }
 
-// Stages x (n fp16 values, 16-byte aligned) as word fragments, and the
-// per-group constants (off, sum x) for groups of WPG*32; xs_in, if given,
-// supplies the per-32 sums of x for the bias term.  All threads of the CTA;
-// no barrier inside (the caller syncs).
+// Stages x (n fp16 values, 16-byte aligned) as word fragments in the XWin
+// layout (zero fragments included), and the per-group constants (off, sum x)
+// for groups of WPG*32; xs_in, if given, supplies the per-32 sums of x for
+// the bias term.  All threads of the CTA; no barrier inside (the caller syncs).
 template <int WPG>
 __device__ __forceinline__ void stage_x(const uint4* __restrict__ x, int n,
                                         const float* __restrict__ xs_in, uint4* xf, float2* gc) {
-    for (int i = threadIdx.x; i < n / 8; i += blockDim.x) xf[i] = frag_of(ld_ro(x + i));
+    using XW = XWin<WPG>;
+    for (int i = threadIdx.x; i < n / 8; i += blockDim.x) {
+        const int w = i / XW::WORDS;
+        xf[w * XW::STRIDE + (i - w * XW::WORDS)] = frag_of(ld_ro(x + i));
+    }
+    const int nwin = n / (256 * WPG) + 1;
+    for (int i = threadIdx.x; i < nwin * WPG; i += blockDim.x)
+        xf[(i / WPG) * XW::STRIDE + XW::WORDS + i % WPG] = make_uint4(0, 0, 0, 0);
     const int ng = n / (32 * WPG);
     for (int G = threadIdx.x; G < ng; G += blockDim.x) {
         float e = 0.f, o = 0.f;
