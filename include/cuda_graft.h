@@ -211,7 +211,8 @@ int graft_moe_fused_down_combine_at(const void* pool, const uint32_t* idx, const
 typedef struct {
     uint32_t* idx;   /* [top_k] selected experts                           */
     float* wgt;      /* [top_k] softmax weights                            */
-    uint32_t* local; /* [1 + top_k] count and slots of resident experts    */
+    uint32_t* local; /* [1 + 2*top_k] count, slots and pool indices of the
+                        selected experts this rank holds                     */
     void* xh;        /* fp16 [hidden]                                      */
     void* h;         /* fp16 [top_k][inter]                                */
     float* xsh;      /* [top_k * inter/32]                                 */

@@ -104,6 +104,11 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
     const uint32_t srow = (uint32_t)(nch / WPG) * SG::ES;
 
     if (threadIdx.x == 0) {
+        prefetch_tmap(&a.wmap);
+        if (a.scale_map) {
+            prefetch_tmap(&a.smap);
+            if (SG::NARR == 2) prefetch_tmap(&a.bmap);
+        }
         for (int i = 0; i < NW * kDepth; ++i) mbar_init(smem_u32(&bars[i]), kTileArrivals);
         fence_mbar_init();
     }

@@ -107,6 +107,11 @@ __device__ __forceinline__ int tile_row_of(int g) {
     return WPG == 4 ? (g >> 1) + 4 * (g & 1) : (g < 4 ? 2 * g : 2 * (g - 4) + 1);
 }
 
+// Brings a tensor map's descriptor into the TMA unit's cache ahead of use.
+__device__ __forceinline__ void prefetch_tmap(const void* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, int x, int y,
                                             uint32_t bar) {
     asm volatile(
@@ -294,34 +299,60 @@ __device__ __forceinline__ float quad_sum(float v) {
 // Stages x (n fp16 values, 16-byte aligned) as word fragments in the XWin
 // layout (zero fragments included), and the per-group constants (off, sum x)
 // for groups of WPG*32; xs_in, if given, supplies the per-32 sums of x for
-// the bias term.  All threads of the CTA; no barrier inside (the caller syncs).
+// the bias term.  One thread per group.  Split in two so that the loads can
+// be issued ahead of a TMA burst (which would otherwise queue in front of
+// them) and finished after it:  XStage<WPG> st; st.load(...); ...; st.store(...).
+// All threads of the CTA call both; no barrier inside (the caller syncs).
+template <int WPG>
+struct XStage {
+    uint4 v[4 * WPG];
+    __device__ __forceinline__ void load(const uint4* __restrict__ x, int n) {
+        const int G = threadIdx.x;
+        if (G < n / (32 * WPG)) {
+#pragma unroll
+            for (int i = 0; i < 4 * WPG; ++i) v[i] = ld_ro(x + 4 * WPG * G + i);
+        }
+    }
+    __device__ __forceinline__ void store(const uint4* __restrict__ x, int n,
+                                          const float* __restrict__ xs_in, uint4* xf,
+                                          float2* gc) {
+        using XW = XWin<WPG>;
+        const int ng = n / (32 * WPG);
+        for (int G = threadIdx.x; G < ng; G += blockDim.x) {
+            if (G != (int)threadIdx.x) {   // more groups than threads: load here
+#pragma unroll
+                for (int i = 0; i < 4 * WPG; ++i) v[i] = ld_ro(x + 4 * WPG * G + i);
+            }
+            float e = 0.f, o = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4 * WPG; ++i) {
+                const int wd = 4 * WPG * G + i, w = wd / XW::WORDS;
+                const uint4 f = frag_of(v[i]);
+                xf[w * XW::STRIDE + (wd - w * XW::WORDS)] = f;
+                float ei, oi;
+                frag_sums(f, ei, oi);
+                e += ei;
+                o += oi;
+            }
+            float s = e + o;
+            if (xs_in) {
+                s = 0.f;
+                for (int c = 0; c < WPG; ++c) s += xs_in[WPG * G + c];
+            }
+            gc[G] = make_float2(fmaf(1024.f, e, 64.f * o), s);
+        }
+        const int nwin = n / (256 * WPG) + 1;
+        for (int i = threadIdx.x; i < nwin * WPG; i += blockDim.x)
+            xf[(i / WPG) * XW::STRIDE + XW::WORDS + i % WPG] = make_uint4(0, 0, 0, 0);
+    }
+};
+
 template <int WPG>
 __device__ __forceinline__ void stage_x(const uint4* __restrict__ x, int n,
                                         const float* __restrict__ xs_in, uint4* xf, float2* gc) {
-    using XW = XWin<WPG>;
-    for (int i = threadIdx.x; i < n / 8; i += blockDim.x) {
-        const int w = i / XW::WORDS;
-        xf[w * XW::STRIDE + (i - w * XW::WORDS)] = frag_of(ld_ro(x + i));
-    }
-    const int nwin = n / (256 * WPG) + 1;
-    for (int i = threadIdx.x; i < nwin * WPG; i += blockDim.x)
-        xf[(i / WPG) * XW::STRIDE + XW::WORDS + i % WPG] = make_uint4(0, 0, 0, 0);
-    const int ng = n / (32 * WPG);
-    for (int G = threadIdx.x; G < ng; G += blockDim.x) {
-        float e = 0.f, o = 0.f;
-        for (int i = 0; i < 4 * WPG; ++i) {
-            float ei, oi;
-            frag_sums(frag_of(ld_ro(x + 4 * WPG * G + i)), ei, oi);
-            e += ei;
-            o += oi;
-        }
-        float s = e + o;
-        if (xs_in) {
-            s = 0.f;
-            for (int c = 0; c < WPG; ++c) s += xs_in[WPG * G + c];
-        }
-        gc[G] = make_float2(fmaf(1024.f, e, 64.f * o), s);
-    }
+    XStage<WPG> st;
+    st.load(x, n);
+    st.store(x, n, xs_in, xf, gc);
 }
 
 // Bounded wait for a slot phase; false (and an error bit) if it never completes.
