@@ -160,14 +160,21 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
         }
     };
 
-    // The weights are constants of the model: stream them before the previous
-    // kernel on the stream has finished.
-    for (int i = 0; i < kDepth && i < mine; ++i) {
-        issue(iss, i);
+    // The weights are constants of the model: each warp's first unit streams
+    // before the previous kernel on the stream has finished.  The rest of the
+    // ring waits until x's few loads are out, so they do not queue behind it.
+    if (mine > 0) {
+        issue(iss, 0);
         iss.next(a.parts, dtile, dpart);
     }
     pdl_wait();   // x, and the y this grid writes, may belong to the previous kernel
-    stage_x<WPG>(a.x, a.K, a.xs_in, xf, gc);
+    XStage<WPG> xst;
+    xst.load(a.x, a.K);
+    for (int i = 1; i < kDepth && i < mine; ++i) {
+        issue(iss, i);
+        iss.next(a.parts, dtile, dpart);
+    }
+    xst.store(a.x, a.K, a.xs_in, xf, gc);
     __syncthreads();
 
     const int t = lane & 3;
