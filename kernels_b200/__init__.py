@@ -171,3 +171,61 @@ def moe_block_ex(pool, R, x, y, P: MoEParams, fmt: MoEFormat | None, ws: MoEWork
                  stream=None) -> None:
     call("graft_moe_block_ex", _p(pool), _p(R), _p(x), _p(y), C.byref(P),
          C.byref(fmt) if fmt is not None else None, C.byref(ws.scratch), _s(stream))
+
+
+# ----------------------------------------------------------- multi-GPU --
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id() -> bytes:
+    """A fresh communicator id (rank 0); hand the bytes to every rank."""
+    buf = C.create_string_buffer(COMM_ID_BYTES)
+    call("graft_comm_get_unique_id", C.addressof(buf))
+    return buf.raw
+
+
+class Comm:
+    """The ranks' communicator (one per process and GPU, on the current device).
+    Collective: every rank constructs it with the same id."""
+
+    def __init__(self, uid: bytes, nranks: int, rank: int):
+        assert len(uid) == COMM_ID_BYTES
+        self._buf = C.create_string_buffer(uid, COMM_ID_BYTES)
+        self.handle = C.c_void_p()
+        call("graft_comm_init", C.byref(self.handle), C.addressof(self._buf), nranks, rank)
+        self.rank, self.nranks = rank, nranks
+
+    def close(self) -> None:
+        if self.handle:
+            call("graft_comm_destroy", self.handle)
+            self.handle = C.c_void_p()
+
+
+def shard_rows(M_total: int, nranks: int, rank: int) -> tuple[int, int]:
+    """Row block [lo, hi) of rank `rank` in the row-sharded GEMV (equal blocks)."""
+    if M_total % nranks:
+        raise ValueError(f"M={M_total} does not split evenly over {nranks} ranks")
+    m = M_total // nranks
+    return rank * m, (rank + 1) * m
+
+
+def expert_range(n_experts: int, nranks: int, rank: int) -> tuple[int, int]:
+    """Experts [lo, hi) held by rank `rank` in the expert-parallel MoE block."""
+    if n_experts % nranks:
+        raise ValueError(f"{n_experts} experts do not split evenly over {nranks} ranks")
+    e = n_experts // nranks
+    return rank * e, (rank + 1) * e
+
+
+def gemv_int4_sharded(comm: Comm, W, SB, x, y_full, P: GemvParams, stream=None) -> None:
+    """This rank's row shard (P: its M rows) into y_full[rank*M:], then all-gather."""
+    call("graft_gemv_int4_sharded", comm.handle, _p(W), _p(SB), _p(x), _p(y_full), C.byref(P),
+         _s(stream))
+
+
+def moe_block_ep(comm: Comm, pool, R, x, y, P: MoEParams, fmt: MoEFormat | None,
+                 ws: MoEWorkspace, stream=None) -> None:
+    """Expert-parallel block: `pool` holds this rank's experts only; y = full output."""
+    call("graft_moe_block_ep", comm.handle, _p(pool), _p(R), _p(x), _p(y), C.byref(P),
+         C.byref(fmt) if fmt is not None else None, C.byref(ws.scratch), _s(stream))
+

@@ -47,7 +47,8 @@ class MoEFormat(C.Structure):
 
 class MoEScratch(C.Structure):
     _fields_ = [("idx", C.c_void_p), ("wgt", C.c_void_p), ("local", C.c_void_p),
-                ("xh", C.c_void_p), ("h", C.c_void_p), ("xsh", C.c_void_p)]
+                ("xh", C.c_void_p), ("h", C.c_void_p), ("xsh", C.c_void_p),
+                ("ypart", C.c_void_p)]
 
 
 P = C.c_void_p
@@ -82,6 +83,13 @@ SIGNATURES: dict[str, tuple] = {
                                  C.POINTER(MoEScratch), P]),
     "graft_moe_block_noalloc": (INT, [P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEFormat),
                                       P]),
+    "graft_comm_get_unique_id": (INT, [P]),
+    "graft_comm_init": (INT, [C.POINTER(P), P, INT, INT]),
+    "graft_comm_destroy": (INT, [P]),
+    "graft_comm_info": (INT, [P, C.POINTER(INT), C.POINTER(INT)]),
+    "graft_gemv_int4_sharded": (INT, [P, P, P, P, P, C.POINTER(GemvParams), P]),
+    "graft_moe_block_ep": (INT, [P, P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEFormat),
+                                 C.POINTER(MoEScratch), P]),
 }
 
 _lib: C.CDLL | None = None

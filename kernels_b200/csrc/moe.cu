@@ -1026,7 +1026,7 @@ size_t graft_moe_scratch_bytes(const GraftMoEParams* P) {
     if (!P) return 0;
     return align256(P->top_k * 4) * 2 + align256((1 + 2 * P->top_k) * 4) +
            align256((size_t)P->hidden * 2) + align256((size_t)P->top_k * P->inter * 2) +
-           align256((size_t)P->top_k * P->quads_int * 4);
+           align256((size_t)P->top_k * P->quads_int * 4) + align256((size_t)P->hidden * 4);
 }
 
 int graft_moe_scratch_carve(void* base, size_t bytes, const GraftMoEParams* P,
@@ -1044,7 +1044,8 @@ int graft_moe_scratch_carve(void* base, size_t bytes, const GraftMoEParams* P,
     out->local = (uint32_t*)p; p += align256((1 + 2 * P->top_k) * 4);
     out->xh = p;              p += align256((size_t)P->hidden * 2);
     out->h = p;               p += align256((size_t)P->top_k * P->inter * 2);
-    out->xsh = (float*)p;
+    out->xsh = (float*)p;     p += align256((size_t)P->top_k * P->quads_int * 4);
+    out->ypart = (float*)p;
     return GRAFT_OK;
 }
 

@@ -57,12 +57,14 @@ def moe_pool(P, scale_f16: bool = True, has_bias_out: bool = False, act_f16: boo
              seed: int = 0, device="cuda", experts=None):
     """Expert pool (uint8, n_experts * blob) in the MoEParams blob layout, plus the
     router R ([n_experts, hidden], fp16 or fp32).  `experts` limits which expert
-    blobs are filled (the rest stay zero), for expert-parallel shards."""
-    g = _gen(seed, device)
+    blobs are filled (the rest stay zero), for expert-parallel shards.  The router
+    and every expert draw from their own seeded generator, so a shard's experts
+    and the router are the same whichever experts are filled."""
     sdt = torch.float16 if scale_f16 else torch.bfloat16
     pool = torch.zeros(P.n_experts * P.blob, dtype=torch.uint8, device=device)
     H, I = P.hidden, P.inter
     for e in (range(P.n_experts) if experts is None else experts):
+        g = _gen(seed * 1000003 + 1 + e, device)
         base = e * P.blob
         for off, rows, K in ((P.off_gate, I, H), (P.off_up, I, H), (P.off_down, H, I)):
             p = base + off
@@ -75,6 +77,6 @@ def moe_pool(P, scale_f16: bool = True, has_bias_out: bool = False, act_f16: boo
             if has_bias_out:
                 bi = torch.randn(rows, generator=g, device=device).mul_(0.02).to(sdt)
                 pool[p + P.sub_bi: p + P.sub_bi + 2 * rows].view(sdt).copy_(bi)
-    R = torch.randn((P.n_experts, H), generator=g, device=device).mul_(0.02)
+    R = torch.randn((P.n_experts, H), generator=_gen(seed, device), device=device).mul_(0.02)
     R = R.half() if act_f16 else R.float()
     return pool, R

@@ -1,0 +1,79 @@
+"""Worker for tests/test_multi_gpu.py, run under torchrun (one rank per GPU):
+the C-ABI multi-GPU calls against the oracle.  Exits non-zero on a mismatch.
+Not collected by pytest (no test_ prefix)."""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+
+import numpy as np
+
+
+def main() -> int:
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import kernels_b200 as kb
+    import oracle
+    from kernels_b200 import synth
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+    # the id travels over gloo; the work runs on the library's own NCCL communicator
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
+    box = [kb.comm_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    comm = kb.Comm(box[0], world, rank)
+    ok = True
+    try:
+        # row-sharded GEMV: rank r holds rows [r*M, (r+1)*M) of the full matrix
+        Mt, K, G = 2048 * world, 2880, 64
+        full = synth.int4_weights(Mt, K, G, seed=11, device="cpu")
+        lo, hi = kb.shard_rows(Mt, world, rank)
+        W = full["W"][lo:hi].cuda()
+        SB = full["SB"][lo:hi].contiguous().cuda()
+        x = synth.activations(K, seed=12, device="cpu").cuda()
+        y = torch.full((Mt,), float("nan"), dtype=torch.float16, device="cuda")
+        kb.gemv_int4_sharded(comm, W, SB, x, y, kb.gemv_params(hi - lo, K, G))
+        torch.cuda.synchronize()
+        ref = oracle.gemv_int4_sb(full["W"].numpy().view(np.uint32), full["SB"].numpy(),
+                                  x.cpu().numpy(), G)
+        got = y.cpu().numpy().astype(np.float64)
+        rel = float(np.max(np.abs(got - ref)) / np.max(np.abs(ref)))
+        print(f"rank {rank}: sharded gemv max|d|/max|ref| = {rel:.2e}", flush=True)
+        ok &= bool(np.isfinite(got).all()) and rel <= 2e-3
+
+        # expert-parallel MoE: rank r's pool holds experts [r*E/n, (r+1)*E/n)
+        P = kb.moe_params(2880, 2880, 16 * world, 4)
+        e_lo, e_hi = kb.expert_range(P.n_experts, world, rank)
+        pool, R = synth.moe_pool(P, scale_f16=True, has_bias_out=False, act_f16=True, seed=13,
+                                 experts=range(e_lo, e_hi))
+        shard = pool[e_lo * P.blob:e_hi * P.blob]
+        xm = synth.activations(2880, seed=14)
+        fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=False,
+                            n_experts=P.n_experts)
+        ws = kb.MoEWorkspace(P)
+        ym = torch.full((2880,), float("nan"), dtype=torch.float32, device="cuda")
+        kb.moe_block_ep(comm, shard, R, xm, ym, P, fmt, ws)
+        torch.cuda.synchronize()
+        # the oracle needs the whole pool: gather every rank's experts on the host
+        mine = shard.cpu()
+        parts = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(parts, mine)
+        whole = torch.cat(parts).numpy()
+        cfg = oracle.moe_cfg(P, scale_bf16=False, has_bias_out=False, router_f16=True)
+        yref = oracle.moe_block(cfg, whole, R.cpu().numpy().view(np.uint16), xm.cpu().numpy())[4]
+        gm = ym.cpu().numpy()
+        mrel = float(np.linalg.norm(gm - yref) / np.linalg.norm(yref))
+        print(f"rank {rank}: ep moe norm rel = {mrel:.2e}", flush=True)
+        ok &= bool(np.isfinite(gm).all()) and mrel <= 1e-3
+    finally:
+        torch.cuda.synchronize()
+        comm.close()
+        dist.destroy_process_group()
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
