@@ -14,9 +14,12 @@ replays.  Detail entries time the VQ GEMV (config 2), the fused MoE block
 bandwidth ceiling the same way.
 
 Under torchrun (N > 1) each rank holds its own shard: a row block of an N-times
-taller matrix set (weak scaling), and the fp16 outputs of every GEMV are
-all-gathered to every rank each step; `value` is all ranks' bytes over the
-slowest rank's time.
+taller matrix set (weak scaling), and every GEMV is graft_gemv_int4_sharded --
+the rank's rows into its slice of the fp16 output, all-gathered over the
+library's own NCCL communicator -- so every rank ends each step with the full
+outputs; `value` is all ranks' bytes over the slowest rank's time.  Detail
+entries at N > 1: the 201088x2880 lm_head split N ways (config 4, strong
+scaling) and the expert-parallel MoE block (config 3, 128/N experts per GPU).
 
 --impl reference times the reference's own CPU implementation of the path
 (cpuRef, int4-gemv/src/main.mm:64-92, compiled from the reference sources into
@@ -136,6 +139,15 @@ class Timer:
                         self.body(start + i)
             self.graphs[key] = g
         return self.graphs[key]
+
+    def build(self, steps: int) -> None:
+        """Captures every graph that run(steps) replays."""
+        done = 0
+        while done < steps:
+            n = min(self.chunk, steps - done)
+            self._graph(n, done)
+            done += n
+        self.torch.cuda.synchronize()
 
     def run(self, steps: int) -> None:
         done = 0
@@ -306,20 +318,27 @@ def main() -> None:
     # each rank holds a row block of its own copy of every shape (weak scaling)
     sets, xs, ys, Ps = build_sweep(torch, kb, synth, SWEEP, seed_base=7919 * rank)
     bytes_step = sweep_bytes(SWEEP)
-    gathered = None
+    comm = gathered = None
     if world > 1:
-        gathered = [torch.empty(world * M, dtype=torch.float16, device="cuda") for M, _ in SWEEP]
+        box = [kb.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        comm = kb.Comm(box[0], world, rank)
+        # symmetric outputs: the GEMV kernels gather them themselves (peer stores)
+        gathered = [comm.alloc((world * M,), torch.float16) for M, _ in SWEEP]
 
     def step(i):
         c = sets[i % NCOPY]
-        for (W, SB), x, y, P in zip(c, xs, ys, Ps):
-            kb.gemv_int4_sb_f16out(W, SB, x, y, P)
-        if gathered is not None:
-            for y, g in zip(ys, gathered):
-                dist.all_gather_into_tensor(g, y)
+        if comm is None:
+            for (W, SB), x, y, P in zip(c, xs, ys, Ps):
+                kb.gemv_int4_sb_f16out(W, SB, x, y, P)
+        else:
+            for (W, SB), x, g, P in zip(c, xs, gathered, Ps):
+                kb.gemv_int4_sharded(comm, W, SB, x, g, P)
 
     chunk = 200
     timer = Timer(torch, step, chunk)
+    timer.build(args.warmup)   # capture first: ranks then start replaying together
+    barrier()
     timer.run(args.warmup)
     torch.cuda.synchronize()
     uuid = None
@@ -336,6 +355,13 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
     value = world * bytes_step * args.steps / dt / 1e9
+    comm_status = {}
+    if comm is not None:
+        try:
+            comm.status()
+            comm_status["sweep"] = "ok"
+        except Exception as ex:  # a fused call's wait for a peer gave up: the number is invalid
+            comm_status["sweep"] = str(ex)
     gpu_launches = len(SWEEP) * args.steps
 
     # roofline of the dominant kernel: the same launches, achieved = bytes / time
@@ -349,18 +375,32 @@ def main() -> None:
 
     detail = {}
     e2e = None
-    if rank == 0 or world == 1:
-        e2e = measure_e2e(torch, kb, sets, xs, Ps, steps=min(args.steps, 3000))
+    e2e = measure_e2e(torch, kb, sets, xs, Ps, steps=min(args.steps, 3000), comm=comm,
+                      world=world, dist=dist, barrier=barrier)
     if not args.no_detail and world == 1:
         detail = measure_detail(torch, kb, synth, timer_cls=Timer)
         detail["sweep_per_shape"] = measure_per_shape(torch, kb, sets, xs, ys, Ps)
         roofline["frac_of_read_ceiling"] = round(
             achieved / detail["stream_read_ceiling_gbs"], 4)
+    if comm is not None:
+        try:
+            comm.status()
+            comm_status["e2e"] = "ok"
+        except Exception as ex:
+            comm_status["e2e"] = str(ex)
+    if not args.no_detail and world > 1:
+        del sets
+        detail = measure_multi(torch, kb, synth, comm, dist, world, rank, barrier)
+        try:
+            comm.status()
+            comm_status["detail"] = "ok"
+        except Exception as ex:
+            comm_status["detail"] = str(ex)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
         cpu = cpu_baseline_leg()
 
-    del timer
+    del timer          # graphs holding communicator calls go before the communicator
     if rank == 0:
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -372,27 +412,94 @@ def main() -> None:
                        "shapes": [f"{M}x{K}" for M, K in SWEEP], "group": GROUP,
                        "bytes_per_step": bytes_step, "l2": f"inputs larger than L2: {NCOPY} "
                        "rotating weight copies (3.0 GB) per rank",
-                       "parallelism": f"rowshard{world}" if world > 1 else "single",
+                       "parallelism": (f"rowshard{world} + all-gather (graft_gemv_int4_sharded, "
+                                       + ("fused into the GEMV over NVLink peer stores)"
+                                          if comm is not None and comm.fused else "NCCL)")
+                                       if world > 1 else "single"),
                        "timing": f"CUDA events around CUDA-graph replays ({chunk} steps/graph)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
             "gpu_launches": gpu_launches, "detail": detail,
         }
+        if comm is not None:
+            out["comm"] = {"fused": comm.fused, "status": comm_status}
         print(json.dumps(out))
+    if comm is not None:
+        torch.cuda.synchronize()
+        comm.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def measure_e2e(torch, kb, sets, xs, Ps, steps: int) -> dict:
+def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier) -> dict:
+    """N > 1: config 4 (201088x2880 lm_head, rows split N ways, all-gather of the
+    fp16 logits) and config 3 expert-parallel (128/N experts per GPU, all-reduce
+    of y).  Times are the slowest rank's."""
+    d = {}
+
+    def slowest(dt):
+        t = torch.tensor([dt], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    torch.cuda.synchronize()
+    barrier()
+    Mt, K = 201088, 2880
+    lo, hi = kb.shard_rows(Mt, world, rank)
+    ncopy = 4
+    ws = [synth.int4_weights(hi - lo, K, GROUP, seed=100 * c + rank) for c in range(ncopy)]
+    x = synth.activations(K, seed=3)
+    yf = comm.alloc((Mt,), torch.float16)
+    P = kb.gemv_params(hi - lo, K, GROUP)
+    t = Timer(torch, lambda i: kb.gemv_int4_sharded(comm, ws[i % ncopy]["W"], ws[i % ncopy]["SB"],
+                                                    x, yf, P), 200)
+    t.build(200)
+    barrier()
+    t.run(200)
+    steps = 2000
+    dt = slowest(t.time(steps, barrier))
+    nb = sweep_bytes([(Mt, K)])
+    d["config4_lmhead_201088x2880"] = {
+        "us_per_call": round(dt / steps * 1e6, 3), "aggregate_gbs": round(nb * steps / dt / 1e9, 1),
+        "rows_per_rank": hi - lo, "allgather_bytes_per_rank": (hi - lo) * 2,
+        "gather": "fused (peer stores from the GEMV epilogue)" if comm.fused else "NCCL",
+        "scaling": "strong"}
+    del t, ws
+
+    Pm = kb.moe_params(2880, 2880, 128, 4)
+    e_lo, e_hi = kb.expert_range(128, world, rank)
+    pool, R = synth.moe_pool(Pm, scale_f16=True, has_bias_out=False, act_f16=True, seed=0,
+                             experts=range(e_lo, e_hi))
+    shard = pool[e_lo * Pm.blob:e_hi * Pm.blob]
+    xs_ = [synth.activations(2880, seed=s) for s in range(16)]
+    y = torch.empty(2880, dtype=torch.float16, device="cuda")
+    wsp = kb.MoEWorkspace(Pm)
+    fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=True,
+                        n_experts=128)
+    t = Timer(torch, lambda i: kb.moe_block_ep(comm, shard, R, xs_[i % 16], y, Pm, fmt, wsp), 200)
+    t.build(200)
+    barrier()
+    t.run(200)
+    steps = 2000
+    dt = slowest(t.time(steps, barrier))
+    d["moe_config3_ep"] = {"us_per_token": round(dt / steps * 1e6, 3),
+                           "experts_per_gpu": e_hi - e_lo, "allreduce": "fp32 y[2880]"}
+    del t
+    return d
+
+
+def measure_e2e(torch, kb, sets, xs, Ps, steps: int, comm=None, world=1, dist=None,
+                barrier=None) -> dict:
     """Same metric through the C-ABI with host buffers: per step, the x of every
     shape comes in from pinned host memory (one packed copy) and every y goes
-    back (one packed copy)."""
+    back (one packed copy; at N > 1 the all-gathered full outputs)."""
     nx = [x.numel() for x in xs]
-    ny = [P.M for P in Ps]
+    ny = [P.M * world for P in Ps]
     hx = torch.cat([x.cpu() for x in xs]).pin_memory()
     hy = torch.empty(sum(ny), dtype=torch.float16).pin_memory()
     dx = torch.empty(sum(nx), dtype=torch.float16, device="cuda")
-    dy = torch.empty(sum(ny), dtype=torch.float16, device="cuda")
+    dy = (torch.empty(sum(ny), dtype=torch.float16, device="cuda") if comm is None
+          else comm.alloc((sum(ny),), torch.float16))
     xo = [sum(nx[:i]) for i in range(len(nx))]
     yo = [sum(ny[:i]) for i in range(len(ny))]
     dxs = [dx[o:o + n] for o, n in zip(xo, nx)]
@@ -402,18 +509,35 @@ def measure_e2e(torch, kb, sets, xs, Ps, steps: int) -> dict:
         c = sets[i % NCOPY]
         dx.copy_(hx, non_blocking=True)
         for (W, SB), x, y, P in zip(c, dxs, dys, Ps):
-            kb.gemv_int4_sb_f16out(W, SB, x, y, P)
+            if comm is None:
+                kb.gemv_int4_sb_f16out(W, SB, x, y, P)
+            else:
+                kb.gemv_int4_sharded(comm, W, SB, x, y, P)
         hy.copy_(dy, non_blocking=True)
 
+    # fused calls spin-wait for their peers: start every phase with the device
+    # and the ranks idle, so no other rank's collective competes for the SMs
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
     t = Timer(torch, body, 100)
+    t.build(100)
+    if barrier:
+        barrier()
     t.run(100)
-    dt = t.time(steps)
-    nbytes = sweep_bytes(SWEEP)
+    dt = t.time(steps, barrier)
+    if dist is not None:
+        tt = torch.tensor([dt], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dt = float(tt.item())
+    del t
+    nbytes = sweep_bytes(SWEEP) * world
     return {"value": round(nbytes * steps / dt / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2,
             "ms_per_step": round(dt / steps * 1e3, 5),
-            "path": "graft_gemv_int4_sb_f16out via ctypes; one pinned H2D of all x and one "
-                    "D2H of all y per step, inside the timed region"}
+            "path": ("graft_gemv_int4_sb_f16out" if comm is None else "graft_gemv_int4_sharded")
+            + " via ctypes; one pinned H2D of all x and one D2H of all y per step (per rank), "
+              "inside the timed region"}
 
 
 def measure_per_shape(torch, kb, sets, xs, ys, Ps) -> dict:

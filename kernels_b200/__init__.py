@@ -195,8 +195,37 @@ class Comm:
         call("graft_comm_init", C.byref(self.handle), C.addressof(self._buf), nranks, rank)
         self.rank, self.nranks = rank, nranks
 
+    @property
+    def fused(self) -> bool:
+        """True when the ranks run the fused (peer-memory) forms."""
+        return bool(load().graft_comm_fused(self.handle))
+
+    def alloc(self, shape, dtype):
+        """A zeroed symmetric buffer (collective) as a CUDA tensor: outputs of the
+        multi-GPU calls placed in it are gathered by the computing kernel itself."""
+        import math
+        import torch
+        n = math.prod(shape) * torch.empty((), dtype=dtype).element_size()
+        ptr = C.c_void_p()
+        call("graft_comm_alloc", self.handle, n, C.byref(ptr))
+        typestr = {torch.float16: "<f2", torch.float32: "<f4", torch.uint8: "|u1"}[dtype]
+
+        class _Buf:
+            __cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                        "data": (ptr.value, False), "version": 2}
+        t = torch.as_tensor(_Buf(), device="cuda")
+        self._owned = getattr(self, "_owned", []) + [ptr.value]
+        return t
+
+    def status(self) -> None:
+        """Raises GraftError if a fused call's wait for a peer gave up."""
+        call("graft_comm_status", self.handle)
+
     def close(self) -> None:
         if self.handle:
+            for p in getattr(self, "_owned", []):
+                call("graft_comm_free", self.handle, p)
+            self._owned = []
             call("graft_comm_destroy", self.handle)
             self.handle = C.c_void_p()
 

@@ -87,6 +87,10 @@ SIGNATURES: dict[str, tuple] = {
     "graft_comm_init": (INT, [C.POINTER(P), P, INT, INT]),
     "graft_comm_destroy": (INT, [P]),
     "graft_comm_info": (INT, [P, C.POINTER(INT), C.POINTER(INT)]),
+    "graft_comm_alloc": (INT, [P, SIZE, C.POINTER(P)]),
+    "graft_comm_free": (INT, [P, P]),
+    "graft_comm_fused": (INT, [P]),
+    "graft_comm_status": (INT, [P]),
     "graft_gemv_int4_sharded": (INT, [P, P, P, P, P, C.POINTER(GemvParams), P]),
     "graft_moe_block_ep": (INT, [P, P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEFormat),
                                  C.POINTER(MoEScratch), P]),

@@ -25,3 +25,4 @@ def test_sharded_gemv_and_ep_moe_two_ranks(lib):
            "--master-port", "29531", str(root / "tests" / "mp_worker.py")]
     r = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "fused forms on" in r.stdout or "fused forms off" in r.stdout
