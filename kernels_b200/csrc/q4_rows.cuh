@@ -1,6 +1,7 @@
 // q4_rows.cuh -- the register-direct int4 group-affine row-dot engine: loads
-// go straight to registers.  Used where the pipelined engine (q4_pipe.cuh) does
-// not apply: rows longer than 32768 weights, and the MoE passes.
+// go straight to registers.  Used where the tensor-pipe tile engine
+// (q4_mma.cuh) does not apply: group sizes other than 32/64/128, rows too long
+// for its shared memory, MoE shapes it does not take; and by the VQ GEMV.
 //
 // The reference computes, per 32-weight chunk c of a row (int4-gemv/src/kernels.metal:20-30),
 //     y += S[g] * sum_{k in c} q_k x_k  +  B[g] * xs[c],   xs[c] = sum_{k in c} x_k
