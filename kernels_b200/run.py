@@ -3,7 +3,7 @@ the counterpart of the reference harness binaries' flags (int4gemv --M --K --G
 --iters, vqgemv --M --K, moefused --experts), without the round-robin tables.
 
     python -m kernels_b200.run int4 --M 128256 --K 4096 [--G 64] [--iters 5] [--copies 2]
-    python -m kernels_b200.run vq --M 14336 --K 4096
+    python -m kernels_b200.run vq --M 14336 --K 4096 [--s32]
     python -m kernels_b200.run moe [--experts 128] [--top-k 4]
     python -m kernels_b200.run stream --mbytes 1024
 
@@ -28,6 +28,7 @@ def main() -> None:
     ap.add_argument("--top-k", type=int, default=4)
     ap.add_argument("--mbytes", type=int, default=1024)
     ap.add_argument("--f32out", action="store_true")
+    ap.add_argument("--s32", action="store_true", help="vq: per-32 scales (the reference's form)")
     a = ap.parse_args()
 
     import torch
@@ -51,13 +52,14 @@ def main() -> None:
             f = lambda i: kb.gemv_int4_sb_f16out(ws[i % a.copies]["W"], ws[i % a.copies]["SB"],  # noqa
                                                  x, y, P)
     elif a.kernel == "vq":
-        ws = [synth.vq_weights(a.M, a.K, seed=c) for c in range(a.copies)]
+        sg = 32 if a.s32 else a.K
+        ws = [synth.vq_weights(a.M, a.K, seed=c, scale_group=sg) for c in range(a.copies)]
         x = synth.activations(a.K)
         y = torch.empty(a.M, dtype=torch.float16, device="cuda")
         P = kb.vq_params(a.M, a.K)
-        nbytes = a.M * a.K // 2 + 2 * a.M + 1024 + 2 * a.K + 2 * a.M
+        nbytes = a.M * a.K // 2 + ws[0]["S"].numel() * 2 + 1024 + 2 * a.K + 2 * a.M
         f = lambda i: kb.gemv_vq_ex(ws[i % a.copies]["IDX"], ws[i % a.copies]["C"],  # noqa
-                                    ws[i % a.copies]["S"], a.K, x, y, P)
+                                    ws[i % a.copies]["S"], sg, x, y, P)
     elif a.kernel == "moe":
         P = kb.moe_params(2880, 2880, a.experts, a.top_k)
         pool, R = synth.moe_pool(P, scale_f16=True, has_bias_out=False, act_f16=True)
