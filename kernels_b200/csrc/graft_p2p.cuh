@@ -29,6 +29,7 @@
 #pragma once
 #include <cstdint>
 
+#include "async_copy.cuh"
 #include "graft_common.cuh"
 
 namespace graft {
@@ -60,11 +61,6 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 
 __device__ __forceinline__ void red_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
 }
 
 constexpr uint64_t kPeerWaitNs = 4000000000ull;

@@ -355,12 +355,19 @@ __device__ __forceinline__ void stage_x(const uint4* __restrict__ x, int n,
     st.store(x, n, xs_in, xf, gc);
 }
 
-// Bounded wait for a slot phase; false (and an error bit) if it never completes.
+// Wait for a slot phase, bounded in time (2 s); false (and an error bit) if
+// it never completes.
+constexpr uint64_t kTileWaitNs = 2000000000ull;
 __device__ __forceinline__ bool wait_tile(uint32_t bar, uint32_t parity, unsigned* err) {
-    for (uint32_t i = 0; i < (1u << 26); ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    if (err) atomicOr(err, 1u);
-    return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_ns() - t0 > kTileWaitNs) {
+            if (err) atomicOr(err, 1u);
+            return false;
+        }
+    }
+    return true;
 }
 
 }  // namespace dev

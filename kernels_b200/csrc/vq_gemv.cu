@@ -4,32 +4,36 @@
 // Every uint8 index is one random 4-byte codebook read, so what bounds this
 // kernel is the SM's L1/shared data path as much as HBM: a warp-wide lookup
 // of 32 codewords is one 128-byte wavefront, and 2 KB of indices need 64 of
-// them -- against 16 for the index bytes themselves.  The design keeps
-// everything else off that path:
+// them.  The design keeps everything else off that path and off the issue
+// slots:
 //   * the codebook is replicated 32 times (the idea of gemv_vq_replicated,
 //     vq-gemv/src/kernels.metal:145-194): copy l of codeword c sits at byte
 //     c*256 + 4*l, in bank l whatever c, so a warp's 32 lookups are one
-//     wavefront; the replicas start on a 64 KiB boundary of the shared
-//     window, so the full address is one PRMT of the packed indices (index
-//     byte -> bits 8..15) with 4*lane + the boundary (bits 0..7, 16..31);
-//   * indices stream from HBM straight into registers with 32-byte loads
-//     (four lanes per 128-byte line: eight whole lines per instruction);
-//     staging them in shared memory would put them on the data path twice
-//     more;
+//     wavefront.  The replicas sit at a fixed address of the shared window
+//     (kCbAddr, just past the 1 KiB the driver reserves per block), so a
+//     lookup is one PRMT of the packed indices (index byte -> bits 8..15,
+//     4*lane -> bits 0..7) and one load with that constant as its offset;
+//   * indices stream by TMA (one 16-row x 128-byte box per unit, 128-byte
+//     swizzle) into a ring of per-warp shared-memory slots: the copies are in
+//     flight without holding registers, which plain loads of this strided
+//     pattern could not keep up (they stalled near 75% of HBM bandwidth);
 //   * the products run on mma.sync m16n8k16: a looked-up codeword is an fp16
-//     pair, exactly one register of the A operand; B is x, arranged so that
-//     column n of the accumulator receives the products of 32-weight group n
-//     of the unit's window only, so per-32 scales apply once per (row, group)
-//     by all lanes; x stays in registers while a warp works in one window.
+//     pair, exactly one register of the A operand, and B is x:
+//       - one scale per row (the BASELINE form): every column of B holds x,
+//         so each accumulator column is the row's whole dot over the window
+//         and a lane ends the unit with its rows' sums (no shuffles);
+//       - per-32 scales (the reference's form): column n of B holds the x of
+//         32-weight group n only (zeros elsewhere), so the accumulator keeps
+//         the 8 groups apart and each (row, group) scale is applied once.
 //
 // Work unit: 16 rows x one window of 8 groups (256 weights, 128 index bytes
-// per row).  Lane (g, t) (g = lane/4, t = lane%4) loads the 32 bytes of
-// groups 2t and 2t+1 of rows g and g+8.  Step s (0, 1) multiplies groups
-// 2t+s: word i of a group's 16 bytes holds indices 4i..4i+3, and MMA h (0, 1)
-// of word i takes indices 4i+2h and 4i+2h+1 of rows g and g+8 as A (k-pairs t
-// and t+4) against x pairs 4i+2h and 4i+2h+1 of the group as B.  Lane (g, t)
-// feeds column g of B: x of group g in step g - 2t (when that is 0 or 1),
-// zeros otherwise.
+// per row).  Lane (g, t) (g = lane/4, t = lane%4) reads the 32 bytes of
+// groups 2t and 2t+1 of rows g and g+8 from the slot.  Step s (0, 1)
+// multiplies group 2t+s: word i of a group's 16 bytes holds indices
+// 4i..4i+3, and MMA h (0, 1) of word i takes indices 4i+2h and 4i+2h+1 of rows
+// g and g+8 as A (k-pairs t and t+4) against x pairs 4i+2h and 4i+2h+1 of the
+// group as B.  In the per-32 form lane (g, t) feeds column g of B: x of group
+// g in step g - 2t (when that is 0 or 1), zeros otherwise.
 //
 // Each CTA (one per SM) owns a balanced range of 16-row tiles; its units,
 // window-major, are split into contiguous runs, one per warp, so a warp
@@ -52,8 +56,16 @@ namespace {
 
 constexpr int kCbStride = 256;                 // bytes per codeword row of 32 copies (+pad)
 constexpr int kCbBytes = 256 * kCbStride;      // 64 KiB
-constexpr int kCbAlignSlack = 65536 - 16;      // dynamic smem is 16-byte aligned
-constexpr int kVqDepth = 2;                    // units in flight per warp (register ring)
+// Shared-window address of the replicas.  Dynamic shared memory starts at
+// the driver's per-block reservation (1 KiB on sm_100) when a kernel has no
+// static shared memory; the kernel checks that it starts at or below kCbAddr
+// and lays everything else out after the replicas.
+constexpr uint32_t kCbAddr = 1024;
+constexpr uint32_t kCbEnd = kCbAddr + kCbBytes;
+constexpr int kVqHead = 1024;                  // mbarriers
+constexpr int kVqMaxDepth = 4;                 // ring slots per warp, at most
+constexpr int kSlotIdx = kTileRows * 128;      // index bytes of a unit
+constexpr int kSlotScale = kTileRows * 16;     // per-32 scales of a unit (map form)
 
 // x in shared memory: per window, 8 groups of 64 bytes at an 80-byte pitch
 // (so the groups the lanes of one load read sit on distinct bank groups);
@@ -63,11 +75,13 @@ constexpr int kXWin = 8 * kXGroup;
 
 enum VqScale : int {
     kVqRow = 0,      // one fp16 scale per row, S[M]
-    kVq32Pair = 1,   // S[M][K/32], read as fp16 pairs (K/32 even, S 4-byte aligned)
-    kVq32Half = 2    // S[M][K/32], read as single fp16 values
+    kVq32Map = 1,    // S[M][K/32], rows 16-byte strided: 16 x 8 boxes by TMA
+    kVq32Ld = 2      // S[M][K/32], other strides: per-lane loads
 };
 
 struct VqArgs {
+    CUtensorMap imap;   // IDX as {K/8 u32, M}, box {32, 16}, 128-byte swizzle
+    CUtensorMap smap;   // S as {K/32 fp16, M}, box {8, 16} (kVq32Map)
     const uint8_t* IDX;
     const uint32_t* C;
     const uint16_t* S;
@@ -77,13 +91,27 @@ struct VqArgs {
     int nch;        // 32-weight groups per row (K/32)
     int parts;      // windows per row (ceil(nch/8))
     int rows_max;   // rows of the largest CTA range: the cells' row pitch
-    int wide;       // rows 32-byte aligned: 32-byte index loads
+    int depth;      // ring slots per warp
 };
 
-// Dynamic shared memory: slack to the first 64 KiB boundary, the replicas,
-// x windows, cells.
-__host__ __device__ inline int vq_tile_smem(int parts, int rows_max) {
-    return kCbAlignSlack + kCbBytes + parts * kXWin + rows_max * parts * 4;
+// A bounded wait that gave up sets a bit here.
+__device__ unsigned g_vq_err;
+
+// Shared window: the codebook replicas at [kCbAddr, kCbEnd), then barriers,
+// the index ring (1024-aligned, for the swizzle), the scale ring, x windows,
+// cells.  The size is reckoned from shared address 0, so it covers any start
+// of dynamic shared memory at or below kCbAddr.
+__host__ __device__ inline int vq_tile_smem(int nw, int depth, bool smap, int parts,
+                                            int rows_max) {
+    return kCbEnd + 1024 + nw * depth * (kSlotIdx + (smap ? kSlotScale : 0)) + parts * kXWin +
+           rows_max * parts * 4;
+}
+
+__device__ __forceinline__ uint32_t cb_addr(uint32_t w, uint32_t lane4, int j) {
+    uint32_t a;
+    // result bytes: [0] = lane4 (byte 4 of {lane4:w}), [1] = byte j of w, [2],[3] = 0
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(a) : "r"(w), "r"(lane4), "r"(0x5504u | (j << 4)));
+    return a;
 }
 
 __device__ __forceinline__ uint32_t lds32(uint32_t saddr) {
@@ -100,67 +128,28 @@ __device__ __forceinline__ uint4 lds128(uint32_t saddr) {
     return v;
 }
 
-// Codeword of index byte j of w from this lane's replica, the replicas on a
-// 64 KiB boundary: la = boundary | 4*lane, and the address is
-// {la.byte3, la.byte2, byte j of w, la.byte0}.
-__device__ __forceinline__ uint32_t cw64(uint32_t w, uint32_t la, int j) {
-    uint32_t a;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(a) : "r"(w), "r"(la), "r"(0x7604u | (j << 4)));
-    return lds32(a);
+// Codeword of index byte j of w from this lane's replica at cb.
+__device__ __forceinline__ uint32_t cw(uint32_t cb, uint32_t w, uint32_t lane4, int j) {
+    return lds32(cb + cb_addr(w, lane4, j));
 }
 
-// A unit's loads: q[r] = index bytes of groups 2t, 2t+1 of row g (r = 0) or
-// g+8 (words 0..3: group 2t, 4..7: group 2t+1); s[r] = the fp16 scales of
-// those groups (per-32 modes).
-struct VqUnit {
-    U32x8 q[2];
-    uint32_t s[2];
-};
-
-__device__ __forceinline__ void vq_load_row(const uint8_t* row, int c, int nch, bool wide,
-                                            U32x8& q) {
-    if (c + 1 < nch && wide) {
-        q = ld_stream256(row + 16 * c);
-        return;
-    }
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    const uint4 lo = c < nch ? ld_stream(row + 16 * c) : z;
-    const uint4 hi = c + 1 < nch ? ld_stream(row + 16 * c + 16) : z;
-    q.w[0] = lo.x; q.w[1] = lo.y; q.w[2] = lo.z; q.w[3] = lo.w;
-    q.w[4] = hi.x; q.w[5] = hi.y; q.w[6] = hi.z; q.w[7] = hi.w;
+// Same, from the replicas at kCbAddr: the address is an immediate offset.
+__device__ __forceinline__ uint32_t cwk(uint32_t w, uint32_t lane4, int j) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1+1024];" : "=r"(v) : "r"(cb_addr(w, lane4, j)));
+    return v;
 }
+static_assert(kCbAddr == 1024, "cwk's offset");
 
+// Row sums of a unit: r0 for row g, r1 for row g+8.  q0/q1: the unit's index
+// words of rows g / g+8 (x: group 2t, y: group 2t+1 as uint4 pairs); x0/x1:
+// the x this lane feeds in step 0/1.  Per-32 form: sc = fp16 scales of groups
+// 2t, 2t+1 of rows g and g+8, r0/r1 cover this lane's columns only.
 template <int SMODE>
-__device__ __forceinline__ void vq_load(const VqArgs& a, int row0, int part, int g, int t,
-                                        VqUnit& U) {
-    const size_t rb = (size_t)a.K / 2;
-    const int ra = min(row0 + g, a.M - 1), rc = min(row0 + g + 8, a.M - 1);
-    const int c = 8 * part + 2 * t;
-    vq_load_row(a.IDX + (size_t)ra * rb, c, a.nch, a.wide, U.q[0]);
-    vq_load_row(a.IDX + (size_t)rc * rb, c, a.nch, a.wide, U.q[1]);
-    if (SMODE != kVqRow) {
-        const uint16_t* sa = a.S + (size_t)ra * a.nch + c;
-        const uint16_t* sc = a.S + (size_t)rc * a.nch + c;
-        if (SMODE == kVq32Pair) {
-            U.s[0] = c < a.nch ? ld_stream32(sa) : 0u;
-            U.s[1] = c < a.nch ? ld_stream32(sc) : 0u;
-        } else {
-            const uint32_t a0 = c < a.nch ? ld_stream16(sa) : 0u;
-            const uint32_t a1 = c + 1 < a.nch ? ld_stream16(sa + 1) : 0u;
-            const uint32_t c0 = c < a.nch ? ld_stream16(sc) : 0u;
-            const uint32_t c1 = c + 1 < a.nch ? ld_stream16(sc + 1) : 0u;
-            U.s[0] = a0 | (a1 << 16);
-            U.s[1] = c0 | (c1 << 16);
-        }
-    }
-}
-
-// Row sums of a unit: r0 for row g, r1 for row g+8, over this lane's columns
-// 2t, 2t+1 (groups 2t, 2t+1 of the window), per-32 scales applied.  x0/x1:
-// the x this lane feeds in step 0/1 (its group's 32 values, or zeros).
-template <int SMODE>
-__device__ __forceinline__ void vq_unit_dot(const VqUnit& U, uint32_t la, const uint4 (&x0)[4],
-                                            const uint4 (&x1)[4], float& r0, float& r1) {
+__device__ __forceinline__ void vq_unit_dot(const uint4 (&q0)[2], const uint4 (&q1)[2],
+                                            uint32_t lane4, const uint4 (&x0)[4],
+                                            const uint4 (&x1)[4], const uint32_t (&sc)[2],
+                                            float& r0, float& r1) {
     // two independent accumulator chains (MMA h)
     float d[2][4];
 #pragma unroll
@@ -169,42 +158,53 @@ __device__ __forceinline__ void vq_unit_dot(const VqUnit& U, uint32_t la, const 
         for (int q = 0; q < 4; ++q) d[c][q] = 0.f;
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
+        const uint32_t wa[4] = {q0[s].x, q0[s].y, q0[s].z, q0[s].w};
+        const uint32_t wc[4] = {q1[s].x, q1[s].y, q1[s].z, q1[s].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const uint4 xv = s ? x1[i] : x0[i];
-            const uint32_t wa = U.q[0].w[4 * s + i], wc = U.q[1].w[4 * s + i];
-            mma_16816(d[0], cw64(wa, la, 0), cw64(wc, la, 0), cw64(wa, la, 1), cw64(wc, la, 1),
-                      xv.x, xv.y);
-            mma_16816(d[1], cw64(wa, la, 2), cw64(wc, la, 2), cw64(wa, la, 3), cw64(wc, la, 3),
-                      xv.z, xv.w);
+            mma_16816(d[0], cwk(wa[i], lane4, 0), cwk(wc[i], lane4, 0), cwk(wa[i], lane4, 1),
+                      cwk(wc[i], lane4, 1), xv.x, xv.y);
+            mma_16816(d[1], cwk(wa[i], lane4, 2), cwk(wc[i], lane4, 2), cwk(wa[i], lane4, 3),
+                      cwk(wc[i], lane4, 3), xv.z, xv.w);
         }
     }
-    float c[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) c[q] = d[0][q] + d[1][q];
     // accumulator element q: row g + 8*(q >> 1), column 2t + (q & 1)
-    if (SMODE == kVqRow) {
-        r0 = c[0] + c[1];
-        r1 = c[2] + c[3];
+    if (SMODE == kVqRow) {   // every column holds the whole window's dot
+        r0 = d[0][0] + d[1][0];
+        r1 = d[0][2] + d[1][2];
     } else {
-        const float2 sa = __half22float2(*reinterpret_cast<const __half2*>(&U.s[0]));
-        const float2 sc = __half22float2(*reinterpret_cast<const __half2*>(&U.s[1]));
-        r0 = fmaf(sa.x, c[0], sa.y * c[1]);
-        r1 = fmaf(sc.x, c[2], sc.y * c[3]);
+        const float2 sa = __half22float2(*reinterpret_cast<const __half2*>(&sc[0]));
+        const float2 sb = __half22float2(*reinterpret_cast<const __half2*>(&sc[1]));
+        r0 = fmaf(sa.x, d[0][0] + d[1][0], sa.y * (d[0][1] + d[1][1]));
+        r1 = fmaf(sb.x, d[0][2] + d[1][2], sb.y * (d[0][3] + d[1][3]));
     }
 }
 
+// Each warp keeps its own ring of D slots full: lane 0 posts a slot's
+// barrier with the TMA copies of the warp's next unit as soon as the warp has
+// read the slot's previous contents.
 template <int SMODE, bool F16OUT, int NW>
 __global__ void __launch_bounds__(NW * 32, 1) vq_tile_kernel(const __grid_constant__ VqArgs a) {
+    constexpr bool ROW = SMODE == kVqRow, SMAP = SMODE == kVq32Map;
+    constexpr int NT = NW * 32;
+    static_assert(NW * kVqMaxDepth * 8 <= kVqHead, "barriers");
     extern __shared__ __align__(16) uint8_t smem[];
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t cb = (sbase + 0xFFFFu) & ~0xFFFFu;   // the replicas: 64 KiB aligned
-    uint8_t* cbp = smem + (cb - sbase);
-    uint8_t* xs = cbp + kCbBytes;
+    if (sbase > kCbAddr) {   // the layout needs the replicas at kCbAddr
+        if (threadIdx.x == 0) atomicOr(&g_vq_err, 2u);
+        return;
+    }
+    uint8_t* cbp = smem + (kCbAddr - sbase);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (kCbEnd - sbase));
+    uint8_t* ring = smem + (((kCbEnd + kVqHead + 1023) & ~1023u) - sbase);
+    uint8_t* sring = ring + NW * a.depth * kSlotIdx;
+    uint8_t* xs = sring + (SMAP ? NW * a.depth * kSlotScale : 0);
     float* cells = reinterpret_cast<float*>(xs + a.parts * kXWin);   // [window][row]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
+    const int D = a.depth;
     const int tiles = (a.M + kTileRows - 1) / kTileRows;
     const int T0 = (int)((long)blockIdx.x * tiles / gridDim.x);
     const int T1 = (int)((long)(blockIdx.x + 1) * tiles / gridDim.x);
@@ -214,6 +214,22 @@ __global__ void __launch_bounds__(NW * 32, 1) vq_tile_kernel(const __grid_consta
     const int units = T * a.parts;
     const int u0 = (int)((long)warp * units / NW), u1 = (int)((long)(warp + 1) * units / NW);
     const int mine = u1 - u0;
+
+    // the codebook first, before this SM's slot copies occupy its memory path
+    constexpr int CPT = 2048 / NT;
+    uint32_t cv[CPT];
+#pragma unroll
+    for (int k = 0; k < CPT; ++k) cv[k] = __ldg(a.C + ((threadIdx.x + k * NT) >> 3));
+    if (threadIdx.x < NW * D) {
+        const int w = threadIdx.x / D, k = threadIdx.x - w * D;
+        mbar_init(smem_u32(&full[w * kVqMaxDepth + k]), kTileArrivals);
+    }
+    if (threadIdx.x == 0) {
+        prefetch_tmap(&a.imap);
+        if (SMAP) prefetch_tmap(&a.smap);
+    }
+    fence_mbar_init();
+    __syncthreads();
     pdl_launch_dependents();
 
     struct It {
@@ -222,26 +238,29 @@ __global__ void __launch_bounds__(NW * 32, 1) vq_tile_kernel(const __grid_consta
             if (++tile == T) { tile = 0; ++part; }
         }
     };
-    It iss{T > 0 ? u0 % T : 0, T > 0 ? u0 / T : 0}, cmp = iss;
-
-    // the indices are constants of the model: the ring fills before the
-    // previous kernel on the stream has finished
-    VqUnit U[kVqDepth];
-#pragma unroll
-    for (int k = 0; k < kVqDepth; ++k) {
-        if (k < mine) {
-            vq_load<SMODE>(a, r0 + kTileRows * iss.tile, iss.part, g, t, U[k]);
-            iss.next(T);
-        }
+    It iss{u0 % T, u0 / T}, cmp = iss;
+    auto slot = [&](int k) { return smem_u32(ring + (warp * D + k) * kSlotIdx); };
+    auto sslot = [&](int k) { return smem_u32(sring + (warp * D + k) * kSlotScale); };
+    auto bar = [&](int k) { return smem_u32(&full[warp * kVqMaxDepth + k]); };
+    auto issue = [&](const It& u, int k) {
+        const uint32_t dst = slot(k), sdst = SMAP ? sslot(k) : 0u, b = bar(k);
+        const int row0 = r0 + kTileRows * u.tile;
+        if (lane != 0) return;
+        mbar_arrive_expect_tx(b, kSlotIdx + (SMAP ? kSlotScale : 0));
+        fence_proxy_async_smem();
+        tma_load_2d(dst, &a.imap, 32 * u.part, row0, b);
+        if (SMAP) tma_load_2d(sdst, &a.smap, 8 * u.part, row0, b);
+    };
+    // the indices (and scales) are constants of the model: the ring fills
+    // before the previous kernel on the stream has finished
+    for (int k = 0; k < D && k < mine; ++k) {
+        issue(iss, k);
+        iss.next(T);
     }
     // codebook replicas: chunk j & 7 (four copies) of codeword j >> 3
-    constexpr int CPT = 2048 / (NW * 32);
-    uint32_t cv[CPT];
-#pragma unroll
-    for (int k = 0; k < CPT; ++k) cv[k] = __ldg(a.C + ((threadIdx.x + k * NW * 32) >> 3));
 #pragma unroll
     for (int k = 0; k < CPT; ++k) {
-        const int j = threadIdx.x + k * NW * 32;
+        const int j = threadIdx.x + k * NT;
         *reinterpret_cast<uint4*>(cbp + (j >> 3) * kCbStride + 16 * (j & 7)) =
             make_uint4(cv[k], cv[k], cv[k], cv[k]);
     }
@@ -250,7 +269,7 @@ __global__ void __launch_bounds__(NW * 32, 1) vq_tile_kernel(const __grid_consta
     uint4 xv[XPT];
 #pragma unroll
     for (int k = 0; k < XPT; ++k) {
-        const int j = threadIdx.x + k * NW * 32;
+        const int j = threadIdx.x + k * NT;
         xv[k] = j < a.nch * 4 ? ld_ro(a.x + j) : make_uint4(0, 0, 0, 0);
     }
     auto xslot = [&](int j) {
@@ -259,58 +278,93 @@ __global__ void __launch_bounds__(NW * 32, 1) vq_tile_kernel(const __grid_consta
     };
 #pragma unroll
     for (int k = 0; k < XPT; ++k) {
-        const int j = threadIdx.x + k * NW * 32;
+        const int j = threadIdx.x + k * NT;
         if (j < a.parts * 32) *xslot(j) = xv[k];
     }
-    for (int j = threadIdx.x + XPT * NW * 32; j < a.parts * 32; j += NW * 32)
+    for (int j = threadIdx.x + XPT * NT; j < a.parts * 32; j += NT)
         *xslot(j) = j < a.nch * 4 ? ld_ro(a.x + j) : make_uint4(0, 0, 0, 0);
     __syncthreads();
 
-    const uint32_t la = cb | ((uint32_t)lane << 2);
-    const uint32_t xg = smem_u32(xs) + g * kXGroup;
-    const int sl = g - 2 * t;   // the step in which this lane feeds B (0 or 1), if any
+    const uint32_t lane4 = (uint32_t)lane << 2;
+    // slot offsets of this lane's two 16-byte chunks (groups 2t, 2t+1) of row g
+    // under the 128-byte swizzle (chunk c of line l at c ^ (l % 8)); row g+8 is
+    // 1024 bytes on, with the same pattern
+    const uint32_t p0 = (uint32_t)((2 * t) ^ (g & 7));
+    const uint32_t o_lo = g * 128 + 16 * p0, o_hi = g * 128 + 16 * (p0 ^ 1u);
+    // x this lane feeds: per row scale, group 2t+s (every lane); per-32
+    // scales, group g in step g - 2t
+    const int sl = g - 2 * t;
+    const uint32_t xg0 = smem_u32(xs) + (ROW ? 2 * t : g) * kXGroup;
+    const uint32_t xg1 = smem_u32(xs) + (ROW ? 2 * t + 1 : g) * kXGroup;
     uint4 x0[4], x1[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) x0[i] = x1[i] = make_uint4(0, 0, 0, 0);
     int xpart = -1;
-    for (int i = 0; i < mine; i += kVqDepth) {
+    bool live = true;   // a wait that gave up: flag it once, read the slots as they are
+    int k = 0;
+    uint32_t ph = 0;
+    for (int i = 0; i < mine; ++i) {
+        if (cmp.part != xpart) {   // warp-uniform: the run entered a new window
+            xpart = cmp.part;
 #pragma unroll
-        for (int k = 0; k < kVqDepth; ++k) {
-            if (i + k < mine) {
-                if (cmp.part != xpart) {   // warp-uniform: the run entered a new window
-                    xpart = cmp.part;
-                    const uint32_t xa = xg + xpart * kXWin;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        if (sl == 0) x0[q] = lds128(xa + 16 * q);
-                        if (sl == 1) x1[q] = lds128(xa + 16 * q);
-                    }
-                }
-                float v0, v1;
-                vq_unit_dot<SMODE>(U[k], la, x0, x1, v0, v1);
-                if (i + k + kVqDepth < mine) {
-                    vq_load<SMODE>(a, r0 + kTileRows * iss.tile, iss.part, g, t, U[k]);
-                    iss.next(T);
-                }
-                v0 = quad_sum(v0);
-                v1 = quad_sum(v1);
-                if (t == 0) {
-                    const int lrow = kTileRows * cmp.tile + g;   // CTA-local rows g and g+8
-                    float* cw = cells + cmp.part * a.rows_max + lrow;
-                    if (r0 + lrow < r1) cw[0] = v0;
-                    if (r0 + lrow + 8 < r1) cw[8] = v1;
-                }
-                cmp.next(T);
+            for (int q = 0; q < 4; ++q) {
+                if (ROW || sl == 0) x0[q] = lds128(xg0 + xpart * kXWin + 16 * q);
+                if (ROW || sl == 1) x1[q] = lds128(xg1 + xpart * kXWin + 16 * q);
             }
         }
+        uint32_t sc[2] = {0u, 0u};
+        if (SMODE == kVq32Ld) {
+            const int row0 = r0 + kTileRows * cmp.tile, c = 8 * cmp.part + 2 * t;
+            const int ra = min(row0 + g, a.M - 1), rc = min(row0 + g + 8, a.M - 1);
+            const uint16_t* sa = a.S + (size_t)ra * a.nch + c;
+            const uint16_t* sb = a.S + (size_t)rc * a.nch + c;
+            sc[0] = (c < a.nch ? ld_stream16(sa) : 0u) |
+                    ((c + 1 < a.nch ? (uint32_t)ld_stream16(sa + 1) : 0u) << 16);
+            sc[1] = (c < a.nch ? ld_stream16(sb) : 0u) |
+                    ((c + 1 < a.nch ? (uint32_t)ld_stream16(sb + 1) : 0u) << 16);
+        }
+        if (live) live = wait_tile(bar(k), ph, &g_vq_err);
+        const uint32_t sa = slot(k);
+        const uint4 q0[2] = {lds128(sa + o_lo), lds128(sa + o_hi)};
+        const uint4 q1[2] = {lds128(sa + 1024 + o_lo), lds128(sa + 1024 + o_hi)};
+        if (SMAP) {
+            const uint32_t ss = sslot(k) + g * 16 + 4 * t;
+            sc[0] = lds32(ss);
+            sc[1] = lds32(ss + 128);
+        }
+        __syncwarp();
+        if (i + D < mine) {   // the slot is read: refill it
+            issue(iss, k);
+            iss.next(T);
+        }
+        float v0, v1;
+        vq_unit_dot<SMODE>(q0, q1, lane4, x0, x1, sc, v0, v1);
+        if (!ROW) {
+            v0 = quad_sum(v0);
+            v1 = quad_sum(v1);
+        }
+        // per row scale: the four lanes of a row hold the same sum
+        const int lrow = kTileRows * cmp.tile + g;   // CTA-local rows g and g+8
+        float* cw = cells + cmp.part * a.rows_max + lrow;
+        if ((ROW || t == 0) && r0 + lrow < r1) cw[0] = v0;
+        if ((ROW || t == 0) && r0 + lrow + 8 < r1) cw[8] = v1;
+        cmp.next(T);
+        if (++k == D) { k = 0; ph ^= 1u; }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < r1 - r0; i += NW * 32) {
+    // four threads per row, each over every fourth window, then a fixed tree
+    for (int i0 = 0; i0 < r1 - r0; i0 += NT / 4) {
+        const int i = i0 + (threadIdx.x >> 2), q0 = threadIdx.x & 3;
         float v = 0.f;
-        for (int q = 0; q < a.parts; ++q) v += cells[q * a.rows_max + i];
-        if (SMODE == kVqRow) v *= h2f(a.S[r0 + i]);
-        if (F16OUT) reinterpret_cast<__half*>(a.y)[r0 + i] = __float2half_rn(v);
-        else reinterpret_cast<float*>(a.y)[r0 + i] = v;
+        if (i < r1 - r0)
+            for (int q = q0; q < a.parts; q += 4) v += cells[q * a.rows_max + i];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (q0 == 0 && i < r1 - r0) {
+            if (SMODE == kVqRow) v *= h2f(a.S[r0 + i]);
+            if (F16OUT) reinterpret_cast<__half*>(a.y)[r0 + i] = __float2half_rn(v);
+            else reinterpret_cast<float*>(a.y)[r0 + i] = v;
+        }
     }
 }
 
@@ -321,18 +375,6 @@ __global__ void __launch_bounds__(NW * 32, 1) vq_tile_kernel(const __grid_consta
 // per index.
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-
-__device__ __forceinline__ uint32_t cb_addr(uint32_t w, uint32_t lane4, int j) {
-    uint32_t a;
-    // result bytes: [0] = lane4 (byte 4 of {lane4:w}), [1] = byte j of w, [2],[3] = 0
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(a) : "r"(w), "r"(lane4), "r"(0x5504u | (j << 4)));
-    return a;
-}
-
-// Codeword of index byte j of w from this lane's replica at cb.
-__device__ __forceinline__ uint32_t cw(uint32_t cb, uint32_t w, uint32_t lane4, int j) {
-    return lds32(cb + cb_addr(w, lane4, j));
-}
 
 // 16 indices (one uint4) against 32 activations (4 uint4 of fp16 pairs).
 __device__ __forceinline__ float vq_chunk(uint4 iv, const uint4 (&xq)[4], uint32_t cb_base,
@@ -481,6 +523,7 @@ int launch_tiles_nw(const VqArgs& a, int grid, int smem, cudaStream_t st) {
 
 template <int SMODE, bool F16OUT>
 int dispatch_vq(VqArgs a, cudaStream_t st) {
+    constexpr int NW = 16;
     DeviceInfo di;
     int rc = current_device_info(&di);
     if (rc) return rc;
@@ -488,15 +531,35 @@ int dispatch_vq(VqArgs a, cudaStream_t st) {
     a.parts = (a.nch + kWindow - 1) / kWindow;
     const int tiles = (a.M + kTileRows - 1) / kTileRows;
     const int grid = std::max(1, std::min(di.sm_count, tiles));
-    const int rows_max = kTileRows * ((tiles + grid - 1) / grid);
-    a.rows_max = rows_max;
-    a.wide = aligned(a.IDX, 32) && a.K % 64 == 0;
-    const int smem = vq_tile_smem(a.parts, rows_max);
-    if (smem <= di.max_smem_optin)
-        return launch_tiles_nw<SMODE, F16OUT, 16>(a, grid, smem, st);
-    constexpr bool ROW = SMODE == kVqRow;
-    if ((long)(a.M + 1) / 2 >= 12L * di.sm_count) return launch_rows<2, 4, ROW, F16OUT>(a, di, st);
-    return launch_rows<1, 4, ROW, F16OUT>(a, di, st);
+    a.rows_max = kTileRows * ((tiles + grid - 1) / grid);
+    constexpr bool SMAP = SMODE == kVq32Map;
+    a.depth = 0;
+    for (int d = kVqMaxDepth; d >= 2 && !a.depth; --d)
+        if (vq_tile_smem(NW, d, SMAP, a.parts, a.rows_max) <= di.max_smem_optin) a.depth = d;
+    if (!a.depth) {   // cells or x too large for the tile engine
+        constexpr bool ROW = SMODE == kVqRow;
+        if ((long)(a.M + 1) / 2 >= 12L * di.sm_count)
+            return launch_rows<2, 4, ROW, F16OUT>(a, di, st);
+        return launch_rows<1, 4, ROW, F16OUT>(a, di, st);
+    }
+    {
+        const uint64_t dims[2] = {(uint64_t)a.K / 8, (uint64_t)a.M};
+        const uint64_t strides[1] = {(uint64_t)a.K / 2};
+        const uint32_t box[2] = {32, kTileRows};
+        if ((rc = encode_tiled(&a.imap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, a.IDX, dims, strides,
+                               box, CU_TENSOR_MAP_SWIZZLE_128B)))
+            return rc;
+    }
+    if (SMAP) {
+        const uint64_t dims[2] = {(uint64_t)a.nch, (uint64_t)a.M};
+        const uint64_t strides[1] = {(uint64_t)a.nch * 2};
+        const uint32_t box[2] = {8, kTileRows};
+        if ((rc = encode_tiled(&a.smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.S, dims, strides, box,
+                               CU_TENSOR_MAP_SWIZZLE_NONE)))
+            return rc;
+    }
+    return launch_tiles_nw<SMODE, F16OUT, NW>(
+        a, grid, vq_tile_smem(NW, a.depth, SMAP, a.parts, a.rows_max), st);
 }
 
 int validate_vq(const void* IDX, const void* Cb, const void* S, const void* x, const void* y,
@@ -538,10 +601,10 @@ int graft_gemv_vq_ex(const void* IDX, const void* Cb, const void* S, uint32_t sc
     a.K = (int)P->K;
     if (rowscale)
         return y_f16 ? dispatch_vq<kVqRow, true>(a, st) : dispatch_vq<kVqRow, false>(a, st);
-    const bool pair = (P->K / 32) % 2 == 0 && aligned(S, 4);
-    if (pair)
-        return y_f16 ? dispatch_vq<kVq32Pair, true>(a, st) : dispatch_vq<kVq32Pair, false>(a, st);
-    return y_f16 ? dispatch_vq<kVq32Half, true>(a, st) : dispatch_vq<kVq32Half, false>(a, st);
+    const bool smap = (P->K / 32) % 8 == 0 && aligned(S, 16);
+    if (smap)
+        return y_f16 ? dispatch_vq<kVq32Map, true>(a, st) : dispatch_vq<kVq32Map, false>(a, st);
+    return y_f16 ? dispatch_vq<kVq32Ld, true>(a, st) : dispatch_vq<kVq32Ld, false>(a, st);
 }
 
 int graft_gemv_vq_wide(const void* IDX, const void* Cb, const void* S, const void* x, float* y,
