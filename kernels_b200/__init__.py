@@ -23,7 +23,8 @@ from ._lib import (GemvParams, GraftError, MoEFormat, MoEParams, MoEScratch, VQP
 __all__ = [
     "GemvParams", "VQParams", "MoEParams", "MoEFormat", "MoEScratch", "GraftError",
     "load", "version", "gemv_params", "xsum32", "gemv_int4_wide_unroll", "gemv_int4_fused",
-    "gemv_int4_simd", "gemv_int4_sb_f16out", "stream_read", "vq_params", "gemv_vq_wide",
+    "gemv_int4_simd", "gemv_int4_sb_f16out", "stream_read", "set_gemv_engine", "get_gemv_engine",
+    "ENGINE_TENSOR", "ENGINE_CUDA_CORE", "vq_params", "gemv_vq_wide",
     "gemv_vq_ex", "vq_decode", "moe_params", "moe_router_topk", "moe_fused_gate_up_swiglu",
     "moe_fused_down_combine", "moe_fused_gate_up_swiglu_at", "moe_fused_down_combine_at",
     "MoEWorkspace", "moe_block", "moe_block_ex", "moe_format",
@@ -82,6 +83,22 @@ def stream_read(src, sink, nquads: int, stream=None) -> None:
 
 
 # --------------------------------------------------------------------- VQ --
+ENGINE_TENSOR, ENGINE_CUDA_CORE = 0, 1
+_ENGINES = {"tensor": ENGINE_TENSOR, "cuda-core": ENGINE_CUDA_CORE}
+
+
+def set_gemv_engine(engine) -> None:
+    """Selects the engine of the dense GEMVs (int4 and VQ), process-wide:
+    "tensor" (default: TMA-fed mma.sync tiles) or "cuda-core" (register-direct
+    fp32 FMAs, no tensor cores)."""
+    call("graft_set_gemv_engine", _ENGINES.get(engine, engine))
+
+
+def get_gemv_engine() -> str:
+    e = load().graft_get_gemv_engine()
+    return {v: k for k, v in _ENGINES.items()}[e]
+
+
 def vq_params(M: int, K: int, cb_size: int = 256) -> VQParams:
     return VQParams(M, K, K // 32, cb_size)
 

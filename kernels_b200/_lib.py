@@ -67,6 +67,8 @@ SIGNATURES: dict[str, tuple] = {
     "graft_gemv_int4_simd": (INT, [P, P, P, P, P, P, C.POINTER(GemvParams), P]),
     "graft_gemv_int4_sb_f16out": (INT, [P, P, P, P, C.POINTER(GemvParams), P]),
     "graft_stream_read": (INT, [P, P, U64, P]),
+    "graft_set_gemv_engine": (INT, [INT]),
+    "graft_get_gemv_engine": (INT, []),
     "graft_gemv_vq_wide": (INT, [P, P, P, P, P, C.POINTER(VQParams), P]),
     "graft_gemv_vq_ex": (INT, [P, P, P, U32, P, P, INT, C.POINTER(VQParams), P]),
     "graft_vq_decode": (INT, [P, P, P, U64, P]),
