@@ -38,24 +38,6 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
-// Non-blocking probe: true if phase `parity` of the mbarrier has completed.
-__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Plain arrive (release at CTA scope) on an mbarrier.
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
 // One bounded probe of phase `parity`; true once that phase has completed.
 // The thread may sleep in the probe (up to ~0.1 ms) until the phase completes,
 // so a waiting warp does not spin on issue slots.

@@ -323,11 +323,9 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_gate_up_mma(
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mtiles = a.inter / kTileRows, upi = 2 * parts;
     const uint32_t srow = (uint32_t)(nch / WPG) * 2;
-    if (threadIdx.x == 0) {
-        prefetch_tmap(&mp.gu);
-        for (int i = 0; i <= NW * kDepth; ++i) mbar_init(smem_u32(&bars[i]), 1);
-        fence_mbar_init();
-    }
+    if (threadIdx.x == 0) prefetch_tmap(&mp.gu);
+    if (threadIdx.x <= NW * kDepth) mbar_init(smem_u32(&bars[threadIdx.x]), 1);
+    fence_mbar_init();
     pdl_wait();                 // idx, local and xh come from the router
     pdl_launch_dependents();    // the selection is final: the down pass may start
     // x first: its few loads must not queue behind the code stream
@@ -481,11 +479,9 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
     const uint32_t srow = (uint32_t)(nch / WPG) * 2;
     const int tiles = a.hidden / kTileRows;
     const int T0 = (int)((long)cid * tiles / ncl), nt = (int)((long)(cid + 1) * tiles / ncl) - T0;
-    if (threadIdx.x == 0) {
-        prefetch_tmap(&mp.dn);
-        for (int i = 0; i <= NW * kDepth; ++i) mbar_init(smem_u32(&bars[i]), 1);
-        fence_mbar_init();
-    }
+    if (threadIdx.x == 0) prefetch_tmap(&mp.dn);
+    if (threadIdx.x <= NW * kDepth) mbar_init(smem_u32(&bars[threadIdx.x]), 1);
+    fence_mbar_init();
     // idx, wgt and local are final before this grid can launch: the gate/up
     // grid lets it launch only after its own wait on the router
     if (warp == 0) fill_slot_table(tab, a, idx, local, lane);
