@@ -17,14 +17,15 @@ from __future__ import annotations
 
 import ctypes as C
 
-from ._lib import (GemvParams, GraftError, MoEFormat, MoEParams, MoEScratch, VQParams, call,
-                   load)
+from ._lib import (ExpertParams, ExpertScratch, GemvParams, GraftError, MoEFormat, MoEParams,
+                   MoEScratch, VQParams, call, load)
 
 __all__ = [
     "GemvParams", "VQParams", "MoEParams", "MoEFormat", "MoEScratch", "GraftError",
     "load", "version", "gemv_params", "xsum32", "gemv_int4_wide_unroll", "gemv_int4_fused",
     "gemv_int4_simd", "gemv_int4_sb_f16out", "stream_read", "set_gemv_engine", "get_gemv_engine",
-    "ENGINE_TENSOR", "ENGINE_CUDA_CORE", "vq_params", "gemv_vq_wide",
+    "ENGINE_TENSOR", "ENGINE_CUDA_CORE", "expert_params", "xsum32_f32", "gemv_int4_bf16",
+    "ExpertScratchBuffers", "expert_forward", "ExpertStream", "vq_params", "gemv_vq_wide",
     "gemv_vq_ex", "vq_decode", "moe_params", "moe_router_topk", "moe_fused_gate_up_swiglu",
     "moe_fused_down_combine", "moe_fused_gate_up_swiglu_at", "moe_fused_down_combine_at",
     "MoEWorkspace", "moe_block", "moe_block_ex", "moe_format",
@@ -97,6 +98,83 @@ def set_gemv_engine(engine) -> None:
 def get_gemv_engine() -> str:
     e = load().graft_get_gemv_engine()
     return {v: k for k, v in _ENGINES.items()}[e]
+
+
+def expert_params(M: int, K: int, G: int) -> ExpertParams:
+    P = ExpertParams()
+    call("graft_expert_params", M, K, G, C.byref(P))
+    return P
+
+
+def xsum32_f32(x, xs, P: ExpertParams, stream=None) -> None:
+    call("graft_xsum32_f32", _p(x), _p(xs), C.byref(P), _s(stream))
+
+
+def gemv_int4_bf16(W, S, B, BI, x, y, xs, P: ExpertParams, stream=None) -> None:
+    """gemv_int4_bf16 (moe-pipeline/src/kernels.metal:53-83), buffers in the reference's order."""
+    call("graft_gemv_int4_bf16", _p(W), _p(S), _p(B), _p(BI), _p(x), _p(y), _p(xs), C.byref(P),
+         _s(stream))
+
+
+class ExpertScratchBuffers:
+    """fp32 scratch of expert_forward, owned by torch."""
+
+    def __init__(self, P: MoEParams, device="cuda"):
+        import torch
+        f = dict(dtype=torch.float32, device=device)
+        self.xs_x = torch.empty(P.hidden // 32, **f)
+        self.gate = torch.empty(P.inter, **f)
+        self.up = torch.empty(P.inter, **f)
+        self.h = torch.empty(P.inter, **f)
+        self.xs_h = torch.empty(P.inter // 32, **f)
+        self.s = ExpertScratch(_p(self.xs_x), _p(self.gate), _p(self.up), _p(self.h),
+                               _p(self.xs_h))
+
+
+def expert_forward(blob, x, y, P: MoEParams, scratch: ExpertScratchBuffers, stream=None) -> None:
+    """One expert (encode_expert, moe-pipeline/src/main.mm:201-239); blob is a device
+    tensor or address holding one experts.bin blob."""
+    call("graft_expert_forward", blob if isinstance(blob, int) else _p(blob), _p(x), _p(y),
+         C.byref(P), C.byref(scratch.s), _s(stream))
+
+
+class ExpertStream:
+    """Slots of device memory filled from pinned host memory on a side stream
+    (graft_expert_stream_*)."""
+
+    def __init__(self, slots, n_slots: int, blob: int):
+        self._slots = slots
+        self.n_slots, self.blob = n_slots, blob
+        h = C.c_void_p()
+        call("graft_expert_stream_create", _p(slots), n_slots, blob, C.byref(h))
+        self._h = h
+
+    def slot(self, s: int) -> int:
+        return load().graft_expert_stream_slot(self._h, s)
+
+    def fetch(self, s: int, host_blob) -> None:
+        call("graft_expert_stream_fetch", self._h, s,
+             host_blob if isinstance(host_blob, int) else _p(host_blob))
+
+    def acquire(self, s: int, stream=None) -> None:
+        call("graft_expert_stream_acquire", self._h, s, _s(stream))
+
+    def release(self, s: int, stream=None) -> None:
+        call("graft_expert_stream_release", self._h, s, _s(stream))
+
+    def sync(self) -> None:
+        call("graft_expert_stream_sync", self._h)
+
+    def close(self) -> None:
+        if self._h:
+            call("graft_expert_stream_destroy", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def vq_params(M: int, K: int, cb_size: int = 256) -> VQParams:

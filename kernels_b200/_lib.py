@@ -51,6 +51,17 @@ class MoEScratch(C.Structure):
                 ("ypart", C.c_void_p)]
 
 
+class ExpertParams(C.Structure):
+    """ExpertParams, moe-pipeline/src/main.mm:53."""
+    _fields_ = [("M", C.c_uint32), ("K", C.c_uint32), ("G", C.c_uint32),
+                ("quads_pr", C.c_uint32), ("groups_pr", C.c_uint32), ("chunks_pg", C.c_uint32)]
+
+
+class ExpertScratch(C.Structure):
+    _fields_ = [("xs_x", C.c_void_p), ("gate", C.c_void_p), ("up", C.c_void_p),
+                ("h", C.c_void_p), ("xs_h", C.c_void_p)]
+
+
 P = C.c_void_p
 U32 = C.c_uint32
 U64 = C.c_uint64
@@ -67,6 +78,17 @@ SIGNATURES: dict[str, tuple] = {
     "graft_gemv_int4_simd": (INT, [P, P, P, P, P, P, C.POINTER(GemvParams), P]),
     "graft_gemv_int4_sb_f16out": (INT, [P, P, P, P, C.POINTER(GemvParams), P]),
     "graft_stream_read": (INT, [P, P, U64, P]),
+    "graft_expert_params": (INT, [U32, U32, U32, C.POINTER(ExpertParams)]),
+    "graft_xsum32_f32": (INT, [P, P, C.POINTER(ExpertParams), P]),
+    "graft_gemv_int4_bf16": (INT, [P, P, P, P, P, P, P, C.POINTER(ExpertParams), P]),
+    "graft_expert_stream_create": (INT, [P, U32, U64, C.POINTER(P)]),
+    "graft_expert_stream_destroy": (INT, [P]),
+    "graft_expert_stream_slot": (P, [P, U32]),
+    "graft_expert_stream_fetch": (INT, [P, U32, P]),
+    "graft_expert_stream_acquire": (INT, [P, U32, P]),
+    "graft_expert_stream_release": (INT, [P, U32, P]),
+    "graft_expert_stream_sync": (INT, [P]),
+    "graft_expert_forward": (INT, [P, P, P, C.POINTER(MoEParams), C.POINTER(ExpertScratch), P]),
     "graft_set_gemv_engine": (INT, [INT]),
     "graft_get_gemv_engine": (INT, []),
     "graft_gemv_vq_wide": (INT, [P, P, P, P, P, C.POINTER(VQParams), P]),

@@ -306,22 +306,34 @@ __device__ __forceinline__ float quad_sum(float v) {
 template <int WPG>
 struct XStage {
     uint4 v[4 * WPG];
-    __device__ __forceinline__ void load(const uint4* __restrict__ x, int n) {
+    // 8 fp16 values of x as one 16-byte word: x16 as given, or x32 rounded
+    __device__ __forceinline__ static uint4 word(const uint4* __restrict__ x16,
+                                                 const float* __restrict__ x32, int i) {
+        if (!x32) return ld_ro(x16 + i);
+        const float4 a = __ldg(reinterpret_cast<const float4*>(x32) + 2 * i);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(x32) + 2 * i + 1);
+        __half2 h[4] = {__floats2half2_rn(a.x, a.y), __floats2half2_rn(a.z, a.w),
+                        __floats2half2_rn(b.x, b.y), __floats2half2_rn(b.z, b.w)};
+        return *reinterpret_cast<uint4*>(h);
+    }
+    // x16: fp16 activations, or x32 (if non-null): fp32 activations, rounded to fp16
+    __device__ __forceinline__ void load(const uint4* __restrict__ x, int n,
+                                         const float* __restrict__ x32 = nullptr) {
         const int G = threadIdx.x;
         if (G < n / (32 * WPG)) {
 #pragma unroll
-            for (int i = 0; i < 4 * WPG; ++i) v[i] = ld_ro(x + 4 * WPG * G + i);
+            for (int i = 0; i < 4 * WPG; ++i) v[i] = word(x, x32, 4 * WPG * G + i);
         }
     }
     __device__ __forceinline__ void store(const uint4* __restrict__ x, int n,
                                           const float* __restrict__ xs_in, uint4* xf,
-                                          float2* gc) {
+                                          float2* gc, const float* __restrict__ x32 = nullptr) {
         using XW = XWin<WPG>;
         const int ng = n / (32 * WPG);
         for (int G = threadIdx.x; G < ng; G += blockDim.x) {
             if (G != (int)threadIdx.x) {   // more groups than threads: load here
 #pragma unroll
-                for (int i = 0; i < 4 * WPG; ++i) v[i] = ld_ro(x + 4 * WPG * G + i);
+                for (int i = 0; i < 4 * WPG; ++i) v[i] = word(x, x32, 4 * WPG * G + i);
             }
             float e = 0.f, o = 0.f;
 #pragma unroll

@@ -73,7 +73,8 @@ __device__ __forceinline__ void stage_act_f16(const uint4* __restrict__ x, int K
 // as the reference's router pass does for the MoE input, moe-fused/src/kernels.metal:137).
 __device__ __forceinline__ void stage_act_f32(const float* __restrict__ x, int K,
                                               uint4* __restrict__ xsm,
-                                              ChunkMeta* __restrict__ meta) {
+                                              ChunkMeta* __restrict__ meta,
+                                              const float* __restrict__ xs_in = nullptr) {
     const int n16 = K >> 3;
     for (int i = threadIdx.x; i < n16; i += blockDim.x) {
         const float4* p = reinterpret_cast<const float4*>(x) + 2 * i;
@@ -102,7 +103,7 @@ __device__ __forceinline__ void stage_act_f32(const float* __restrict__ x, int K
                 o += f.y;
             }
         }
-        meta[c] = ChunkMeta{fmaf(1024.f, e, 64.f * o), e + o};
+        meta[c] = ChunkMeta{fmaf(1024.f, e, 64.f * o), xs_in ? xs_in[c] : e + o};
     }
     __syncthreads();
 }

@@ -45,6 +45,9 @@ def lib() -> C.CDLL:
         L.oracle_vq_decode.argtypes = [_P, _P, _P, _U64]
         L.oracle_moe_block.argtypes = [_P, _P, _P, _P, _P, _P, _P, _P, _P, _INT]
         L.oracle_moe_block.restype = _INT
+        L.oracle_gemv_int4_bf16.argtypes = [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _INT]
+        L.oracle_expert_forward.argtypes = [_P, _P, _P, _P, _INT]
+        L.oracle_expert_forward.restype = _INT
         L.cpu_fast_gemv_int4_sb.argtypes = [_P, _P, _P, _P, _U32, _U32, _U32, _INT]
         L.cpu_fast_gemv_int4_sb.restype = _INT
         _lib = L
@@ -198,3 +201,24 @@ def ref_moe_block(P, pool, R, x):
                     P.off_gate, P.off_up, P.off_down, P.sub_w, P.sub_s, P.sub_b, P.sub_bi,
                     _ptr(idx), _ptr(wgt), _ptr(logits), _ptr(y))
     return idx, wgt, logits, y
+
+
+def gemv_int4_bf16(W, S, B, BI, x, G: int, nthreads: int = 0) -> np.ndarray:
+    """fp64 y of gemv_int4_bf16 (moe-pipeline/src/kernels.metal:53-83): bf16 S, B, BI,
+    fp32 x."""
+    M, K = W.shape[0], W.shape[1] * 8
+    y = np.empty(M, np.float64)
+    lib().oracle_gemv_int4_bf16(_ptr(np.ascontiguousarray(W)), _ptr(_u16(S)), _ptr(_u16(B)),
+                                _ptr(_u16(BI)), _ptr(np.ascontiguousarray(x, np.float32)),
+                                _ptr(y), M, K, G, nthreads)
+    return y
+
+
+def expert_forward(cfg: MoECfg, blob: np.ndarray, x: np.ndarray, nthreads: int = 0):
+    """fp64 y of one expert (moe-pipeline/src/main.mm:201-239) from fp32 x."""
+    y = np.empty(cfg.hidden, np.float64)
+    rc = lib().oracle_expert_forward(C.byref(cfg), _ptr(np.ascontiguousarray(blob)),
+                                     _ptr(np.ascontiguousarray(x, np.float32)), _ptr(y), nthreads)
+    if rc != 0:
+        raise ValueError("oracle_expert_forward rejected the configuration")
+    return y

@@ -267,4 +267,40 @@ int oracle_moe_block(const OracleMoECfg* c, const uint8_t* pool, const void* R,
     return 0;
 }
 
+// One projection in gpt-oss's on-disk form (bf16 S, B and per-row output bias
+// BI) against fp32 x: gemv_int4_bf16, moe-pipeline/src/kernels.metal:53-83,
+// restated like refProj (moe-fused/src/main.mm:46-62) in fp64.
+void oracle_gemv_int4_bf16(const uint32_t* W, const uint16_t* S, const uint16_t* B,
+                           const uint16_t* BI, const float* x, double* y, uint32_t M,
+                           uint32_t K, uint32_t G, int nthreads) {
+    const uint32_t wpr = K / 8, gpr = K / G;
+    par_rows(M, nthreads, [=](uint32_t m0, uint32_t m1) {
+        for (uint32_t m = m0; m < m1; ++m) {
+            const uint32_t* wr = W + (size_t)m * wpr;
+            double a = 0.0;
+            for (uint32_t k = 0; k < K; ++k) {
+                uint32_t g = k / G;
+                a += (bf2d(S[(size_t)m * gpr + g]) * (double)nib(wr, k)
+                      + bf2d(B[(size_t)m * gpr + g])) * (double)x[k];
+            }
+            y[m] = a + bf2d(BI[m]);
+        }
+    });
+}
+
+// One expert as moe-pipeline's encode_expert computes it
+// (moe-pipeline/src/main.mm:201-239): gate and up of fp32 x, gpt-oss SwiGLU,
+// down of h; fp64 throughout.
+int oracle_expert_forward(const OracleMoECfg* c, const uint8_t* blob, const float* x,
+                          double* y, int nthreads) {
+    const uint32_t H = c->hidden, I = c->inter;
+    std::vector<double> xd(H), g(I), u(I), h(I);
+    for (uint32_t k = 0; k < H; ++k) xd[k] = (double)x[k];
+    moe_proj(c, blob, c->off_gate, xd.data(), g.data(), I, H, nthreads);
+    moe_proj(c, blob, c->off_up, xd.data(), u.data(), I, H, nthreads);
+    for (uint32_t i = 0; i < I; ++i) h[i] = swiglu(g[i], u[i]);
+    moe_proj(c, blob, c->off_down, h.data(), y, H, I, nthreads);
+    return 0;
+}
+
 }  // extern "C"
