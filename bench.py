@@ -584,6 +584,82 @@ def measure_vq(torch, kb, synth, timer_cls) -> dict:
     return vq
 
 
+def measure_expert_stream(torch, kb, synth, n_exp: int = 24, depth: int = 2,
+                          reps: int = 3) -> dict:
+    """moe-pipeline on B200: gpt-oss experts (14,024,704 B, bf16 scales + output bias)
+    streamed from pinned host memory into HBM slots on a side stream while each is
+    computed (graft_expert_*).  Drivers as the reference's (moe-pipeline/src/main.mm:
+    299-363): `seq` copy-then-compute, `io` copies only (the ceiling), `pipe` depth-d
+    refill-before-compute; wall time around the run, best of `reps`."""
+    import time
+    P = kb.moe_params(2880, 2880, n_exp, 4)
+    pool, _ = synth.moe_pool(P, scale_f16=False, has_bias_out=True, act_f16=False, seed=11)
+    host = torch.empty(pool.numel(), dtype=torch.uint8, pin_memory=True)
+    host.copy_(pool)
+    del pool
+    blob, ns = P.blob, depth + 2
+    slots = torch.empty(ns * blob, dtype=torch.uint8, device="cuda")
+    es = kb.ExpertStream(slots, ns, blob)
+    scratch = kb.ExpertScratchBuffers(P)
+    x = synth.activations(2880, seed=3).float()
+    y = torch.empty(2880, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream()
+    hp = host.data_ptr()
+
+    def seq():
+        for i in range(n_exp):
+            es.fetch(0, hp + i * blob)
+            es.acquire(0, st)
+            kb.expert_forward(es.slot(0), x, y, P, scratch, st)
+            es.release(0, st)
+
+    def io():
+        for i in range(n_exp):
+            es.fetch(i % ns, hp + i * blob)
+
+    def pipe():
+        for i in range(min(depth, n_exp)):
+            es.fetch(i % ns, hp + i * blob)
+        for i in range(n_exp):
+            s = i % ns
+            es.acquire(s, st)
+            if i + depth < n_exp:
+                es.fetch((i + depth) % ns, hp + (i + depth) * blob)
+            kb.expert_forward(es.slot(s), x, y, P, scratch, st)
+            es.release(s, st)
+
+    out = {}
+    for name, fn in (("seq", seq), ("io", io), ("pipe", pipe)):
+        best = 1e30
+        for _ in range(reps + 1):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            fn()
+            es.sync()
+            torch.cuda.synchronize()
+            best = min(best, time.perf_counter() - t0)
+        out[name] = {"ms": round(best * 1e3, 3), "gbs": round(n_exp * blob / best / 1e9, 2)}
+    # compute alone, over resident slots
+    io()
+    es.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(40):
+        kb.expert_forward(es.slot(i % ns), x, y, P, scratch, st)
+    e1.record()
+    torch.cuda.synchronize()
+    comp_us = e0.elapsed_time(e1) * 1e3 / 40
+    es.close()
+    del host, slots
+    out.update({"experts": n_exp, "blob_bytes": blob, "depth": depth, "slots": ns,
+                "compute_us_per_expert": round(comp_us, 2),
+                "compute_gbs": round(blob / comp_us / 1e3, 1),
+                "pipe_over_io": round(out["io"]["ms"] / out["pipe"]["ms"], 4),
+                "pipe_over_seq": round(out["seq"]["ms"] / out["pipe"]["ms"], 3),
+                "source": "pinned host memory (the reference streams from SSD)"})
+    return out
+
+
 def measure_detail(torch, kb, synth, timer_cls) -> dict:
     d = {}
     # read-only ceiling over the same kind of rotation (8 x 1 GB)
@@ -596,6 +672,7 @@ def measure_detail(torch, kb, synth, timer_cls) -> dict:
     del bufs
 
     d["vq_config2"] = measure_vq(torch, kb, synth, timer_cls)
+    d["expert_stream"] = measure_expert_stream(torch, kb, synth)
 
     # MoE config 3 (gpt-oss-120b shape, 128 experts, top-4, BASELINE format)
     P = kb.moe_params(2880, 2880, 128, 4)
