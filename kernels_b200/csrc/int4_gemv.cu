@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(64) xsum32_f32_kernel(const float4* __restrict
 __device__ unsigned g_int4_err;
 
 struct GemvArgs {
-    CUtensorMap wmap;       // codes {K/8 words, M rows}, box {32, 16}, 128-byte swizzle
+    CUtensorMap wmap;       // codes {K/8 words, M rows}, box {32, 16}, 128-byte swizzle; or
+                            // (map3) {32 words, M rows, K/256 segments}, box {32, 16, WPG}
     CUtensorMap smap;       // scales {groups, M}, box {8, 16} (map mode)
     CUtensorMap bmap;       // biases, separate layout (map mode)
     const uint8_t* S;       // interleaved pairs, or separate scales
@@ -90,6 +91,7 @@ struct GemvArgs {
     int scap;               // bytes per scale array region of a slot
     const P2PGather* gather;   // fused all-gather of y (fp16), or null
     long y_off;                // element offset of this rank's rows in the gathered y
+    int map3;                  // wmap is 3-D (K % 256 == 0): one copy per unit, not one per segment
     const float* x32;          // fp32 activations (rounded to fp16 when staged), or null
     const uint16_t* BI;        // bf16 per-row output bias added to y, or null
 };
@@ -233,10 +235,15 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
             if (SG::NARR == 2) sc1 = span_copy(sd + a.scap, a.B + so, (uint32_t)nrow * srow, a.b_end);
             bytes += sc0.bytes + sc1.bytes;
         }
+        if (a.map3) bytes += (uint32_t)(WPG - nseg) * kTileRows * 128;   // the full box
         mbar_arrive_expect_tx(bar, bytes);
         fence_proxy_async_smem();
-        for (int sg = 0; sg < nseg; ++sg)
-            tma_load_2d(cd + sg * kTileRows * 128, &a.wmap, 4 * c0 + 32 * sg, row0, bar);
+        if (a.map3) {
+            tma_load_3d(cd, &a.wmap, 0, row0, c0 / 8, bar);
+        } else {
+            for (int sg = 0; sg < nseg; ++sg)
+                tma_load_2d(cd + sg * kTileRows * 128, &a.wmap, 4 * c0 + 32 * sg, row0, bar);
+        }
         if (a.scale_map) {
             tma_load_2d(sd, &a.smap, g0, row0, bar);
             if (SG::NARR == 2) tma_load_2d(sd + a.scap, &a.bmap, g0, row0, bar);
@@ -497,12 +504,27 @@ int launch_tiles(GemvArgs a, const DeviceInfo& di, cudaStream_t st, bool* fits) 
 
     int rc;
     {
-        const uint64_t dims[2] = {(uint64_t)a.K / 8, (uint64_t)a.M};
-        const uint64_t strides[1] = {(uint64_t)a.K / 2};
-        const uint32_t box[2] = {32, kTileRows};
-        if ((rc = encode_tiled(&a.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, a.W, dims, strides, box,
-                               CU_TENSOR_MAP_SWIZZLE_128B)))
-            return rc;
+        // Rows of whole 128-byte segments: the segment is a third dimension
+        // (stride 128 B) and one box brings a unit's WPG segments in the
+        // [segment][row][128 B] order of the slot -- half (or a quarter of) the
+        // copies, which the TMA unit issues at a bounded rate.  Every in-range
+        // coordinate stays inside W.
+        a.map3 = a.K % 256 == 0;
+        if (a.map3) {
+            const uint64_t dims[3] = {32, (uint64_t)a.M, (uint64_t)a.K / 256};
+            const uint64_t strides[2] = {(uint64_t)a.K / 2, 128};
+            const uint32_t box[3] = {32, kTileRows, (uint32_t)WPG};
+            if ((rc = encode_tiled(&a.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, a.W, dims, strides,
+                                   box, CU_TENSOR_MAP_SWIZZLE_128B)))
+                return rc;
+        } else {
+            const uint64_t dims[2] = {(uint64_t)a.K / 8, (uint64_t)a.M};
+            const uint64_t strides[1] = {(uint64_t)a.K / 2};
+            const uint32_t box[2] = {32, kTileRows};
+            if ((rc = encode_tiled(&a.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, a.W, dims, strides,
+                                   box, CU_TENSOR_MAP_SWIZZLE_128B)))
+                return rc;
+        }
     }
     if (a.scale_map) {
         const CUtensorMapDataType dt =
