@@ -180,6 +180,14 @@ __global__ void __launch_bounds__(kThreads) moe_router_kernel(
     }
     float my_val = -INFINITY;
     uint32_t my_idx = 0;
+    // The warp-wide step is two reductions: the largest value (as an
+    // order-preserving key; -0 counts as +0, as '>' does), then the lowest
+    // index holding it.  A lane's candidate is its own first maximum, so the
+    // pick is the reference's first maximum overall.
+    auto key = [](float f) {
+        const uint32_t b = __float_as_uint(f == 0.f ? 0.f : f);
+        return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    };
 #pragma unroll
     for (int j = 0; j < kMaxTopK; ++j) {
         if (j >= top_k) break;
@@ -188,13 +196,10 @@ __global__ void __launch_bounds__(kThreads) moe_router_kernel(
 #pragma unroll
         for (int t = 0; t < kMaxExperts / 32; ++t)
             if (v[t] > bv) { bv = v[t]; bi = lane + 32 * t; }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        if (bi == 0x7fffffff) bi = 0;  // nothing above -inf: the reference keeps index 0
+        const uint32_t kb = key(bv), kmax = __reduce_max_sync(0xffffffffu, kb);
+        bi = (int)__reduce_min_sync(0xffffffffu, kb == kmax ? (uint32_t)bi : 0x7fffffffu);
+        bv = __shfl_sync(0xffffffffu, bv, bi & 31);   // the value itself, from its lane
+        if (bi == 0x7fffffff) { bi = 0; bv = -INFINITY; }   // nothing above -inf: index 0
         if (lane == j) { my_val = bv; my_idx = (uint32_t)bi; }
 #pragma unroll
         for (int t = 0; t < kMaxExperts / 32; ++t)
@@ -273,8 +278,15 @@ __device__ __forceinline__ void fill_slot_table(SlotTable* t, const MoEArgs& a,
 }
 
 struct MoEMaps {
-    CUtensorMap gu;   // gate/up codes
-    CUtensorMap dn;   // down codes
+    CUtensorMap gu;   // gate/up codes {hidden/8 words, inter rows, 2 proj, experts}
+    CUtensorMap dn;   // down codes {inter/8 words, hidden rows, experts}
+    // The same codes with the 128-byte segment as a dimension (stride 128 B):
+    // one box brings a unit's two whole segments, in the slot's
+    // [segment][row][128 B] order.  Units that reach the rows' partial last
+    // segment use the maps above.
+    CUtensorMap gu5;  // {32 words, inter rows, hidden/256 segments, 2 proj, experts}
+    CUtensorMap dn4;  // {32 words, hidden rows, inter/256 segments, experts}
+    int gu_segs, dn_segs;   // whole segments per row covered by gu5 / dn4 (0: maps unused)
 };
 
 // Stages `n` scale row blocks: block b is 16 rows of `srow` bytes at src(b),
@@ -379,9 +391,13 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_gate_up_mma(
         if (lane != 0) return;
         mbar_arrive_expect_tx(bar, (uint32_t)nseg * kTileRows * 128);
         fence_proxy_async_smem();
-        for (int sg = 0; sg < nseg; ++sg)
-            tma_load_4d(cd + sg * kTileRows * 128, &mp.gu, 4 * c0 + 32 * sg, itm.y * kTileRows, proj,
-                        itm.z, bar);
+        if (c0 / 8 + WPG <= mp.gu_segs) {
+            tma_load_5d(cd, &mp.gu5, 0, itm.y * kTileRows, c0 / 8, proj, itm.z, bar);
+        } else {
+            for (int sg = 0; sg < nseg; ++sg)
+                tma_load_4d(cd + sg * kTileRows * 128, &mp.gu, 4 * c0 + 32 * sg,
+                            itm.y * kTileRows, proj, itm.z, bar);
+        }
     };
     for (int i = 0; i < kDepth && i < mine; ++i) {
         issue(iss, i);
@@ -517,9 +533,13 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
         if (lane != 0) return;
         mbar_arrive_expect_tx(bar, (uint32_t)nseg * kTileRows * 128);
         fence_proxy_async_smem();
-        for (int sg = 0; sg < nseg; ++sg)
-            tma_load_3d(cd + sg * kTileRows * 128, &mp.dn, 4 * c0 + 32 * sg,
-                        (T0 + u.k) * kTileRows, tab->le[p], bar);
+        if (c0 / 8 + WPG <= mp.dn_segs) {
+            tma_load_4d(cd, &mp.dn4, 0, (T0 + u.k) * kTileRows, c0 / 8, tab->le[p], bar);
+        } else {
+            for (int sg = 0; sg < nseg; ++sg)
+                tma_load_3d(cd + sg * kTileRows * 128, &mp.dn, 4 * c0 + 32 * sg,
+                            (T0 + u.k) * kTileRows, tab->le[p], bar);
+        }
     };
     // the down rows first: they do not depend on the gate/up pass
     for (int i = 0; i < kDepth && i < mine; ++i) {
@@ -832,6 +852,31 @@ bool mma_maps(const MoEArgs& a, MoEMaps* mp) {
         if (encode_tiled(&mp->dn, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, dbase, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B))
             return false;
+    }
+    // segment-dimension views (every in-range coordinate stays inside its row)
+    mp->gu_segs = (int)(a.hidden / 256);
+    if (mp->gu_segs >= 2) {
+        const uint64_t dims[5] = {32, (uint64_t)a.inter, (uint64_t)mp->gu_segs, 2,
+                                  (uint64_t)a.n_local};
+        const uint64_t strides[4] = {(uint64_t)a.hidden / 2, 128, a.off_up - a.off_gate, a.blob};
+        const uint32_t box[5] = {32, kTileRows, 2, 1, 1};
+        if (encode_tiled(&mp->gu5, CU_TENSOR_MAP_DATA_TYPE_UINT32, 5, gbase, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+            mp->gu_segs = 0;
+    } else {
+        mp->gu_segs = 0;
+    }
+    mp->dn_segs = (int)(a.inter / 256);
+    if (mp->dn_segs >= 2) {
+        const uint64_t dims[4] = {32, (uint64_t)a.hidden, (uint64_t)mp->dn_segs,
+                                  (uint64_t)a.n_local};
+        const uint64_t strides[3] = {(uint64_t)a.inter / 2, 128, a.blob};
+        const uint32_t box[4] = {32, kTileRows, 2, 1};
+        if (encode_tiled(&mp->dn4, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, dbase, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+            mp->dn_segs = 0;
+    } else {
+        mp->dn_segs = 0;
     }
     graft::clear_error();   // a rejected map only means the fallback passes run
     return true;

@@ -135,6 +135,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int x
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* map, int x, int y, int z,
+                                            int w, int v, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z),
+        "r"(w), "r"(v), "r"(bar)
+        : "memory");
+}
+
 // One 1-D bulk copy of bytes [p, p + n) of an array ending at `end`, as the
 // 16-byte-aligned span around it, into shared `dst` (the span start lands at
 // dst).  Where the span would pass the array end, the aligned part goes by
