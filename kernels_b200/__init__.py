@@ -24,6 +24,7 @@ __all__ = [
     "GemvParams", "VQParams", "MoEParams", "MoEFormat", "MoEScratch", "GraftError",
     "load", "version", "gemv_params", "xsum32", "gemv_int4_wide_unroll", "gemv_int4_fused",
     "gemv_int4_simd", "gemv_int4_sb_f16out", "stream_read", "set_gemv_engine", "get_gemv_engine",
+    "device_errors",
     "ENGINE_TENSOR", "ENGINE_CUDA_CORE", "expert_params", "xsum32_f32", "gemv_int4_bf16",
     "ExpertScratchBuffers", "expert_forward", "ExpertStream", "vq_params", "gemv_vq_wide",
     "gemv_vq_ex", "vq_decode", "moe_params", "moe_router_topk", "moe_fused_gate_up_swiglu",
@@ -93,6 +94,14 @@ def set_gemv_engine(engine) -> None:
     "tensor" (default: TMA-fed mma.sync tiles) or "cuda-core" (register-direct
     fp32 FMAs, no tensor cores)."""
     call("graft_set_gemv_engine", _ENGINES.get(engine, engine))
+
+
+def device_errors(clear: bool = False) -> dict:
+    """The kernels' device-side error bits (graft_device_errors), per kernel file."""
+    b = C.c_uint32()
+    call("graft_device_errors", C.byref(b), int(clear))
+    v = b.value
+    return {"int4": v & 0xFF, "vq": (v >> 8) & 0xFF, "moe": (v >> 16) & 0xFF}
 
 
 def get_gemv_engine() -> str:

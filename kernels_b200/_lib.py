@@ -89,6 +89,7 @@ SIGNATURES: dict[str, tuple] = {
     "graft_expert_stream_release": (INT, [P, U32, P]),
     "graft_expert_stream_sync": (INT, [P]),
     "graft_expert_forward": (INT, [P, P, P, C.POINTER(MoEParams), C.POINTER(ExpertScratch), P]),
+    "graft_device_errors": (INT, [C.POINTER(U32), INT]),
     "graft_set_gemv_engine": (INT, [INT]),
     "graft_get_gemv_engine": (INT, []),
     "graft_gemv_vq_wide": (INT, [P, P, P, P, P, C.POINTER(VQParams), P]),

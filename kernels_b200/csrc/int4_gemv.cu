@@ -741,3 +741,22 @@ int graft_stream_read(const void* src, uint32_t* sink, uint64_t nquads, graft_st
 }
 
 }  // extern "C"
+
+namespace graft {
+
+// Error bits the kernels of this file set on the device (a time-bounded wait
+// that gave up, a failed layout check); read, and cleared if asked.
+unsigned int4_device_errors(bool clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_int4_err, sizeof v) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_int4_err, &z, sizeof z);
+    }
+    return v;
+}
+
+}  // namespace graft

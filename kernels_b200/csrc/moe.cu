@@ -1250,3 +1250,22 @@ extern "C" int graft_moe_block_noalloc(const void* pool, const void* R, const vo
     if ((rc = graft_moe_scratch_carve(base, kNoAllocScratchBytes, P, &s))) return rc;
     return graft_moe_block_ex(pool, R, x, y, P, fmt, &s, stream);
 }
+
+namespace graft {
+
+// Error bits the kernels of this file set on the device (a time-bounded wait
+// that gave up, a failed layout check); read, and cleared if asked.
+unsigned moe_device_errors(bool clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_moe_err, sizeof v) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_moe_err, &z, sizeof z);
+    }
+    return v;
+}
+
+}  // namespace graft

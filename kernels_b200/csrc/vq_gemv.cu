@@ -625,3 +625,22 @@ int graft_vq_decode(const void* IDX, const void* Cb, void* out, uint64_t n_idx,
 }
 
 }  // extern "C"
+
+namespace graft {
+
+// Error bits the kernels of this file set on the device (a time-bounded wait
+// that gave up, a failed layout check); read, and cleared if asked.
+unsigned vq_device_errors(bool clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_vq_err, sizeof v) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_vq_err, &z, sizeof z);
+    }
+    return v;
+}
+
+}  // namespace graft

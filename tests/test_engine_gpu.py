@@ -64,3 +64,4 @@ def test_vq_cuda_core(cuda_core, M, K, sg):
     ref = oracle.gemv_vq(host(w["IDX"]), host(w["C"]).view(np.uint16), S, sgv,
                          host(x).view(np.uint16))
     assert norm_rel(host(y), ref) <= TOL
+
