@@ -23,7 +23,7 @@ from ._lib import (ExpertParams, ExpertScratch, GemvParams, GraftError, MoEForma
 __all__ = [
     "GemvParams", "VQParams", "MoEParams", "MoEFormat", "MoEScratch", "GraftError",
     "load", "version", "gemv_params", "xsum32", "gemv_int4_wide_unroll", "gemv_int4_fused",
-    "gemv_int4_simd", "gemv_int4_sb_f16out", "stream_read", "set_gemv_engine", "get_gemv_engine",
+    "gemv_int4_simd", "gemv_int4_sb_f16out", "gemm_int4_sb_f16", "stream_read", "set_gemv_engine", "get_gemv_engine",
     "device_errors",
     "ENGINE_TENSOR", "ENGINE_CUDA_CORE", "expert_params", "xsum32_f32", "gemv_int4_bf16",
     "ExpertScratchBuffers", "expert_forward", "ExpertStream", "vq_params", "gemv_vq_wide",
@@ -78,6 +78,11 @@ def gemv_int4_simd(W, S, B, x, y, xs, P: GemvParams, stream=None) -> None:
 
 def gemv_int4_sb_f16out(W, SB, x, y, P: GemvParams, stream=None) -> None:
     call("graft_gemv_int4_sb_f16out", _p(W), _p(SB), _p(x), _p(y), C.byref(P), _s(stream))
+
+
+def gemm_int4_sb_f16(W, SB, X, Y, B: int, P: GemvParams, stream=None) -> None:
+    """The int4 GEMV for B = 1..8 tokens at once: X fp16 [B][K], Y fp16 [B][M]."""
+    call("graft_gemm_int4_sb_f16", _p(W), _p(SB), _p(X), _p(Y), B, C.byref(P), _s(stream))
 
 
 def stream_read(src, sink, nquads: int, stream=None) -> None:

@@ -78,6 +78,7 @@ SIGNATURES: dict[str, tuple] = {
     "graft_gemv_int4_simd": (INT, [P, P, P, P, P, P, C.POINTER(GemvParams), P]),
     "graft_gemv_int4_sb_f16out": (INT, [P, P, P, P, C.POINTER(GemvParams), P]),
     "graft_stream_read": (INT, [P, P, U64, P]),
+    "graft_gemm_int4_sb_f16": (INT, [P, P, P, P, U32, C.POINTER(GemvParams), P]),
     "graft_expert_params": (INT, [U32, U32, U32, C.POINTER(ExpertParams)]),
     "graft_xsum32_f32": (INT, [P, P, C.POINTER(ExpertParams), P]),
     "graft_gemv_int4_bf16": (INT, [P, P, P, P, P, P, P, C.POINTER(ExpertParams), P]),
