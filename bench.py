@@ -660,6 +660,30 @@ def measure_expert_stream(torch, kb, synth, n_exp: int = 24, depth: int = 2,
     return out
 
 
+def measure_batch(torch, kb, synth, timer_cls, B: int = 8) -> dict:
+    """graft_gemm_int4_sb_f16 (B tokens per call, weights read once) against B
+    batch-1 calls, on config-1 shapes; 8 rotating weight copies."""
+    out = {}
+    for M, K in [(14336, 4096), (6144, 4096), (128256, 4096)]:
+        n = NCOPY if M * K // 2 * NCOPY > (256 << 20) else 16
+        n = min(n, max(2, int((1 << 30) // (M * K // 2))))
+        ws = [synth.int4_weights(M, K, 64, seed=c) for c in range(n)]
+        X = torch.stack([synth.activations(K, seed=50 + b) for b in range(B)])
+        Y = torch.empty((B, M), dtype=torch.float16, device="cuda")
+        P = kb.gemv_params(M, K, 64)
+        tb = timer_cls(torch, lambda i: kb.gemm_int4_sb_f16(ws[i % n]["W"], ws[i % n]["SB"], X, Y,
+                                                            B, P), 100)
+        tb.run(100)
+        steps = 1000
+        dt = tb.time(steps) / steps
+        wbytes = M * K // 2 + M * (K // 64) * 4
+        out[f"{M}x{K}"] = {"B": B, "us_per_call": round(dt * 1e6, 3),
+                           "tokens_per_s": round(B / dt, 1),
+                           "weight_gbs": round(wbytes / dt / 1e9, 1)}
+        del ws
+    return out
+
+
 def measure_detail(torch, kb, synth, timer_cls) -> dict:
     d = {}
     # read-only ceiling over the same kind of rotation (8 x 1 GB)
@@ -673,6 +697,7 @@ def measure_detail(torch, kb, synth, timer_cls) -> dict:
 
     d["vq_config2"] = measure_vq(torch, kb, synth, timer_cls)
     d["expert_stream"] = measure_expert_stream(torch, kb, synth)
+    d["batched_gemv_b8"] = measure_batch(torch, kb, synth, timer_cls)
 
     # MoE config 3 (gpt-oss-120b shape, 128 experts, top-4, BASELINE format)
     P = kb.moe_params(2880, 2880, 128, 4)
