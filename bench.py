@@ -660,26 +660,36 @@ def measure_expert_stream(torch, kb, synth, n_exp: int = 24, depth: int = 2,
     return out
 
 
-def measure_batch(torch, kb, synth, timer_cls, B: int = 8) -> dict:
-    """graft_gemm_int4_sb_f16 (B tokens per call, weights read once) against B
-    batch-1 calls, on config-1 shapes; 8 rotating weight copies."""
+def measure_batch(torch, kb, synth, timer_cls, batches=(8, 16)) -> dict:
+    """graft_gemm_int4_sb_f16 (B tokens per call, the weights read once) against
+    the batch-1 GEMV on the same matrix, on the config-1 shapes and config 4's
+    201088x2880 lm_head (its batch-8 crossover probe); rotating weight copies
+    larger than L2."""
     out = {}
-    for M, K in [(14336, 4096), (6144, 4096), (128256, 4096)]:
-        n = NCOPY if M * K // 2 * NCOPY > (256 << 20) else 16
-        n = min(n, max(2, int((1 << 30) // (M * K // 2))))
-        ws = [synth.int4_weights(M, K, 64, seed=c) for c in range(n)]
-        X = torch.stack([synth.activations(K, seed=50 + b) for b in range(B)])
-        Y = torch.empty((B, M), dtype=torch.float16, device="cuda")
-        P = kb.gemv_params(M, K, 64)
-        tb = timer_cls(torch, lambda i: kb.gemm_int4_sb_f16(ws[i % n]["W"], ws[i % n]["SB"], X, Y,
-                                                            B, P), 100)
-        tb.run(100)
-        steps = 1000
-        dt = tb.time(steps) / steps
+    for M, K in [(14336, 4096), (6144, 4096), (128256, 4096), (201088, 2880)]:
         wbytes = M * K // 2 + M * (K // 64) * 4
-        out[f"{M}x{K}"] = {"B": B, "us_per_call": round(dt * 1e6, 3),
-                           "tokens_per_s": round(B / dt, 1),
-                           "weight_gbs": round(wbytes / dt / 1e9, 1)}
+        n = max(2, min(16, int((1 << 30) // wbytes)))
+        ws = [synth.int4_weights(M, K, 64, seed=c) for c in range(n)]
+        P = kb.gemv_params(M, K, 64)
+        X = torch.stack([synth.activations(K, seed=50 + b) for b in range(max(batches))])
+        Y = torch.empty((max(batches), M), dtype=torch.float16, device="cuda")
+        steps = 400
+
+        def timed(body):
+            tb = timer_cls(torch, body, 100)
+            tb.run(100)
+            return tb.time(steps) / steps
+
+        d1 = timed(lambda i: kb.gemv_int4_sb_f16out(ws[i % n]["W"], ws[i % n]["SB"], X[0], Y[0],
+                                                    P))
+        e = {"gemv_b1_us": round(d1 * 1e6, 3), "gemv_b1_weight_gbs": round(wbytes / d1 / 1e9, 1)}
+        for B in batches:
+            dt = timed(lambda i, B=B: kb.gemm_int4_sb_f16(ws[i % n]["W"], ws[i % n]["SB"], X, Y,
+                                                          B, P))
+            e[f"b{B}"] = {"us_per_call": round(dt * 1e6, 3), "tokens_per_s": round(B / dt, 1),
+                          "weight_gbs": round(wbytes / dt / 1e9, 1),
+                          "vs_b1_calls": round(B * d1 / dt, 2)}
+        out[f"{M}x{K}"] = e
         del ws
     return out
 
@@ -697,7 +707,7 @@ def measure_detail(torch, kb, synth, timer_cls) -> dict:
 
     d["vq_config2"] = measure_vq(torch, kb, synth, timer_cls)
     d["expert_stream"] = measure_expert_stream(torch, kb, synth)
-    d["batched_gemv_b8"] = measure_batch(torch, kb, synth, timer_cls)
+    d["batched_gemv"] = measure_batch(torch, kb, synth, timer_cls)
 
     # MoE config 3 (gpt-oss-120b shape, 128 experts, top-4, BASELINE format)
     P = kb.moe_params(2880, 2880, 128, 4)

@@ -118,11 +118,11 @@ int graft_gemv_int4_bf16(const void* W, const void* S, const void* B, const void
                          const float* x, float* y, const float* xs, const GraftExpertParams* P,
                          graft_stream_t stream);
 
-/* The interleaved-SB int4 GEMV for B = 1..8 tokens at once (no reference
+/* The interleaved-SB int4 GEMV for B = 1..16 tokens at once (no reference
  * counterpart: the reference decodes one token): X fp16 [B][K] row-major,
  * Y fp16 [B][M] row-major, Y[b] = W . X[b] with fp32 accumulation.  The
  * weights are read once per launch; a launch takes as many tokens as their
- * staged x leaves shared memory for (all 8 up to K = 4096, 3 at K = 14336),
+ * staged x leaves shared memory for (all 16 up to K = 4096, 5 at K = 14336),
  * larger B runs in chunks.  G = 32, 64 or 128; W and X 16-byte aligned. */
 int graft_gemm_int4_sb_f16(const void* W, const void* SB, const void* X, void* Y, uint32_t B,
                            const GraftGemvParams* P, graft_stream_t stream);

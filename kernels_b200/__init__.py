@@ -81,7 +81,7 @@ def gemv_int4_sb_f16out(W, SB, x, y, P: GemvParams, stream=None) -> None:
 
 
 def gemm_int4_sb_f16(W, SB, X, Y, B: int, P: GemvParams, stream=None) -> None:
-    """The int4 GEMV for B = 1..8 tokens at once: X fp16 [B][K], Y fp16 [B][M]."""
+    """The int4 GEMV for B = 1..16 tokens at once: X fp16 [B][K], Y fp16 [B][M]."""
     call("graft_gemm_int4_sb_f16", _p(W), _p(SB), _p(X), _p(Y), B, C.byref(P), _s(stream))
 
 

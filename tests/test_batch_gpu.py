@@ -1,4 +1,4 @@
-"""GPU parity of the batched int4 GEMV (graft_gemm_int4_sb_f16, B = 1..8
+"""GPU parity of the batched int4 GEMV (graft_gemm_int4_sb_f16, B = 1..16
 tokens per call) against the fp64 oracle, token by token."""
 from __future__ import annotations
 
@@ -18,8 +18,8 @@ def host(t):
 
 
 @pytest.mark.parametrize("M,K,G", [(4096, 4096, 64), (14336, 4096, 64), (300, 2880, 32),
-                                   (77, 1024, 128), (1000, 14336, 64)])
-@pytest.mark.parametrize("B", [1, 3, 8])
+                                   (2000, 2880, 64), (77, 1024, 128), (1000, 14336, 64)])
+@pytest.mark.parametrize("B", [1, 3, 8, 12, 16])
 def test_batched_vs_oracle(lib, M, K, G, B):
     import torch
     import kernels_b200 as kb
@@ -61,6 +61,6 @@ def test_batched_rejects_bad_batch(lib):
     P = kb.gemv_params(64, 256, 64)
     t = torch.zeros(4096, dtype=torch.uint8, device="cuda")
     with pytest.raises(kb.GraftError):
-        kb.gemm_int4_sb_f16(t, t, t, t, 9, P)
+        kb.gemm_int4_sb_f16(t, t, t, t, 17, P)
     with pytest.raises(kb.GraftError):
         kb.gemm_int4_sb_f16(t, t, t, t, 0, P)
