@@ -694,6 +694,28 @@ def measure_batch(torch, kb, synth, timer_cls, batches=(8, 16)) -> dict:
     return out
 
 
+def measure_vq_quantize(torch, kb) -> dict:
+    """The VQ quantiser (offline tooling, not on the decode path): one
+    quantisation of a config-2 matrix with the reference's defaults (25 Lloyd
+    passes on 200,000 sampled pairs, 256 codewords), CUDA-event timed after a
+    warm-up run."""
+    out = {}
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for M, K in [(4096, 4096), (14336, 4096)]:
+        W = torch.randn((M, K), generator=g, device="cuda", dtype=torch.float32) * 0.02
+        kb.vq_quantize(W)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        kb.vq_quantize(W)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        out[f"{M}x{K}"] = {"ms": round(ms, 3), "pairs_per_s": round(M * K / 2 / (ms * 1e-3), 1)}
+        del W
+    return out
+
+
 def measure_detail(torch, kb, synth, timer_cls) -> dict:
     d = {}
     # read-only ceiling over the same kind of rotation (8 x 1 GB)
@@ -708,6 +730,7 @@ def measure_detail(torch, kb, synth, timer_cls) -> dict:
     d["vq_config2"] = measure_vq(torch, kb, synth, timer_cls)
     d["expert_stream"] = measure_expert_stream(torch, kb, synth)
     d["batched_gemv"] = measure_batch(torch, kb, synth, timer_cls)
+    d["vq_quantize"] = measure_vq_quantize(torch, kb)
 
     # MoE config 3 (gpt-oss-120b shape, 128 experts, top-4, BASELINE format)
     P = kb.moe_params(2880, 2880, 128, 4)

@@ -188,6 +188,25 @@ int graft_gemv_vq_ex(const void* IDX, const void* C, const void* S, uint32_t sca
 int graft_vq_decode(const void* IDX, const void* C, void* out, uint64_t n_idx,
                     graft_stream_t stream);
 
+/* The VQ quantiser, vq-gemv/quant/pq_quantize.py:50-75 (quantize_matrix, with
+ * _kmeans :28-47): W fp32 [M][K] -> IDX [M][K/2], C fp16 [256][2] and
+ * S fp16 [M][K/32] (max |w| of each 32), the layout graft_gemv_vq_ex reads
+ * with scale_group 32; w ~ S[m][2i/32] * C[IDX[m][i]][t].  Lloyd's k-means
+ * (iters passes, reference 25) on sub sampled normalised pairs (reference
+ * 200000; all pairs if there are fewer).  The sample and the initial
+ * centroids come from seeded splitmix64 draws, not the reference's MLX
+ * generator; the result is deterministic and bit-identical run to run. */
+typedef struct {
+    uint32_t M, K;      /* W rows and columns, K % 32 == 0          */
+    uint32_t iters;     /* Lloyd passes                             */
+    uint32_t sub;       /* sample size, 1 .. 2^22                   */
+    uint64_t seed;
+} GraftVQQuantParams;
+/* Device workspace bytes graft_vq_quantize needs (0 for bad params). */
+uint64_t graft_vq_quantize_workspace(const GraftVQQuantParams* P);
+int graft_vq_quantize(const float* W, void* IDX, void* C, void* S, const GraftVQQuantParams* P,
+                      void* ws, uint64_t ws_bytes, graft_stream_t stream);
+
 /* ============================================================ MoE block ===
  * One decode token through a gpt-oss-style MoE block: router + top-k + softmax,
  * gate/up + SwiGLU, down + weighted combine, in three kernels.

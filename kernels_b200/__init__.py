@@ -18,7 +18,7 @@ from __future__ import annotations
 import ctypes as C
 
 from ._lib import (ExpertParams, ExpertScratch, GemvParams, GraftError, MoEFormat, MoEParams,
-                   MoEScratch, VQParams, call, load)
+                   MoEScratch, VQParams, VQQuantParams, call, load)
 
 __all__ = [
     "GemvParams", "VQParams", "MoEParams", "MoEFormat", "MoEScratch", "GraftError",
@@ -27,7 +27,7 @@ __all__ = [
     "device_errors",
     "ENGINE_TENSOR", "ENGINE_CUDA_CORE", "expert_params", "xsum32_f32", "gemv_int4_bf16",
     "ExpertScratchBuffers", "expert_forward", "ExpertStream", "vq_params", "gemv_vq_wide",
-    "gemv_vq_ex", "vq_decode", "moe_params", "moe_router_topk", "moe_fused_gate_up_swiglu",
+    "gemv_vq_ex", "vq_decode", "vq_quantize", "moe_params", "moe_router_topk", "moe_fused_gate_up_swiglu",
     "moe_fused_down_combine", "moe_fused_gate_up_swiglu_at", "moe_fused_down_combine_at",
     "MoEWorkspace", "moe_block", "moe_block_ex", "moe_format",
 ]
@@ -208,6 +208,25 @@ def gemv_vq_ex(IDX, Cb, S, scale_group: int, x, y, P: VQParams, stream=None) -> 
 
 def vq_decode(IDX, Cb, out, n_idx: int, stream=None) -> None:
     call("graft_vq_decode", _p(IDX), _p(Cb), _p(out), n_idx, _s(stream))
+
+
+def vq_quantize(W, iters: int = 25, sub: int = 200_000, seed: int = 0, stream=None):
+    """The VQ quantiser (vq-gemv/quant/pq_quantize.py:50-75) on the GPU: W fp32
+    [M, K] (device) -> (IDX uint8 [M, K/2], C fp16 [256, 2], S fp16 [M, K/32])."""
+    import torch
+    M, K = W.shape
+    P = VQQuantParams(M, K, iters, sub, seed)
+    nbytes = load().graft_vq_quantize_workspace(C.byref(P))
+    if nbytes == 0:
+        raise GraftError("graft_vq_quantize_workspace", 1,
+                         f"bad parameters (M={M} K={K} sub={sub})")
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=W.device)
+    IDX = torch.empty((M, K // 2), dtype=torch.uint8, device=W.device)
+    Cb = torch.empty((256, 2), dtype=torch.float16, device=W.device)
+    S = torch.empty((M, K // 32), dtype=torch.float16, device=W.device)
+    call("graft_vq_quantize", _p(W), _p(IDX), _p(Cb), _p(S), C.byref(P), _p(ws), nbytes,
+         _s(stream))
+    return IDX, Cb, S
 
 
 # -------------------------------------------------------------------- MoE --

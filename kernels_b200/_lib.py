@@ -28,6 +28,12 @@ class VQParams(C.Structure):
                 ("cb_size", C.c_uint32)]
 
 
+class VQQuantParams(C.Structure):
+    """GraftVQQuantParams: the quantiser's shape, passes, sample size and seed."""
+    _fields_ = [("M", C.c_uint32), ("K", C.c_uint32), ("iters", C.c_uint32),
+                ("sub", C.c_uint32), ("seed", C.c_uint64)]
+
+
 class MoEParams(C.Structure):
     """MoEParams, moe-fused/src/kernels.metal:22-35 (u64 block at byte 40)."""
     _fields_ = [("hidden", C.c_uint32), ("inter", C.c_uint32), ("n_experts", C.c_uint32),
@@ -96,6 +102,8 @@ SIGNATURES: dict[str, tuple] = {
     "graft_gemv_vq_wide": (INT, [P, P, P, P, P, C.POINTER(VQParams), P]),
     "graft_gemv_vq_ex": (INT, [P, P, P, U32, P, P, INT, C.POINTER(VQParams), P]),
     "graft_vq_decode": (INT, [P, P, P, U64, P]),
+    "graft_vq_quantize_workspace": (U64, [C.POINTER(VQQuantParams)]),
+    "graft_vq_quantize": (INT, [P, P, P, P, C.POINTER(VQQuantParams), P, U64, P]),
     "graft_moe_params": (INT, [U32, U32, U32, U32, C.POINTER(MoEParams)]),
     "graft_moe_router_topk": (INT, [P, P, P, P, C.POINTER(MoEParams), P, P, P]),
     "graft_moe_fused_gate_up_swiglu": (INT, [P, P, P, P, C.POINTER(MoEParams), P]),
