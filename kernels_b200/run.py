@@ -6,6 +6,8 @@ the counterpart of the reference harness binaries' flags (int4gemv --M --K --G
     python -m kernels_b200.run vq --M 14336 --K 4096 [--s32]
     python -m kernels_b200.run moe [--experts 128] [--top-k 4]
     python -m kernels_b200.run stream --mbytes 1024
+    python -m kernels_b200.run batch --M 128256 --K 4096 --B 8
+    python -m kernels_b200.run vqquant --M 4096 --K 4096
 
 Each iteration is one launch on a rotating weight copy, timed with CUDA events;
 use it for small profiler captures (a few launches, a few GB).
@@ -18,7 +20,7 @@ import json
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["int4", "vq", "moe", "stream"])
+    ap.add_argument("kernel", choices=["int4", "vq", "moe", "stream", "batch", "vqquant"])
     ap.add_argument("--M", type=int, default=4096)
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--G", type=int, default=64)
@@ -27,6 +29,7 @@ def main() -> None:
     ap.add_argument("--experts", type=int, default=128)
     ap.add_argument("--top-k", type=int, default=4)
     ap.add_argument("--mbytes", type=int, default=1024)
+    ap.add_argument("--B", type=int, default=8, help="batch: tokens per call")
     ap.add_argument("--f32out", action="store_true")
     ap.add_argument("--s32", action="store_true", help="vq: per-32 scales (the reference's form)")
     a = ap.parse_args()
@@ -60,6 +63,19 @@ def main() -> None:
         nbytes = a.M * a.K // 2 + ws[0]["S"].numel() * 2 + 1024 + 2 * a.K + 2 * a.M
         f = lambda i: kb.gemv_vq_ex(ws[i % a.copies]["IDX"], ws[i % a.copies]["C"],  # noqa
                                     ws[i % a.copies]["S"], sg, x, y, P)
+    elif a.kernel == "batch":
+        ws = [synth.int4_weights(a.M, a.K, a.G, seed=c) for c in range(a.copies)]
+        X = torch.stack([synth.activations(a.K, seed=50 + b) for b in range(a.B)])
+        Y = torch.empty((a.B, a.M), dtype=torch.float16, device="cuda")
+        P = kb.gemv_params(a.M, a.K, a.G)
+        nbytes = a.M * a.K // 2 + 4 * a.M * (a.K // a.G) + 2 * a.B * (a.K + a.M)
+        f = lambda i: kb.gemm_int4_sb_f16(ws[i % a.copies]["W"], ws[i % a.copies]["SB"],  # noqa
+                                          X, Y, a.B, P)
+    elif a.kernel == "vqquant":
+        g = torch.Generator(device="cuda").manual_seed(0)
+        W = torch.randn((a.M, a.K), generator=g, device="cuda", dtype=torch.float32) * 0.02
+        nbytes = a.M * a.K * 4
+        f = lambda i: kb.vq_quantize(W)  # noqa
     elif a.kernel == "moe":
         P = kb.moe_params(2880, 2880, a.experts, a.top_k)
         pool, R = synth.moe_pool(P, scale_f16=True, has_bias_out=False, act_f16=True)
