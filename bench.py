@@ -312,6 +312,24 @@ def main() -> None:
     def barrier():
         if dist is not None:
             dist.barrier()
+            # the barrier is an NCCL kernel on its own stream: let it finish before
+            # anything else is enqueued, or a fused call's spinning CTAs may hold
+            # every SM while the peer waits in its barrier for this one
+            torch.cuda.synchronize()
+
+    def status_all(phase: str) -> None:
+        """The communicator status of every rank (a timeout shows on the rank
+        that waited); rank 0 reports the first failure."""
+        try:
+            comm.status()
+            mine = ""
+        except Exception as ex:  # a fused call's wait for a peer gave up: the number is invalid
+            mine = f"rank {rank}: {ex}"
+        got = [None] * world
+        dist.all_gather_object(got, mine)
+        torch.cuda.synchronize()
+        bad = [g for g in got if g]
+        comm_status[phase] = bad[0] if bad else "ok"
 
     kb.load()
     peaks = measured_peaks()
@@ -357,11 +375,7 @@ def main() -> None:
     value = world * bytes_step * args.steps / dt / 1e9
     comm_status = {}
     if comm is not None:
-        try:
-            comm.status()
-            comm_status["sweep"] = "ok"
-        except Exception as ex:  # a fused call's wait for a peer gave up: the number is invalid
-            comm_status["sweep"] = str(ex)
+        status_all("sweep")
     gpu_launches = len(SWEEP) * args.steps
 
     # roofline of the dominant kernel: the same launches, achieved = bytes / time
@@ -392,19 +406,11 @@ def main() -> None:
         roofline["frac_of_read_ceiling"] = round(
             achieved / detail["stream_read_ceiling_gbs"], 4)
     if comm is not None:
-        try:
-            comm.status()
-            comm_status["e2e"] = "ok"
-        except Exception as ex:
-            comm_status["e2e"] = str(ex)
+        status_all("e2e")
     if not args.no_detail and world > 1:
         del sets
-        detail = measure_multi(torch, kb, synth, comm, dist, world, rank, barrier)
-        try:
-            comm.status()
-            comm_status["detail"] = "ok"
-        except Exception as ex:
-            comm_status["detail"] = str(ex)
+        detail = measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status_all)
+        status_all("detail_moe_ep")
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
         cpu = cpu_baseline_leg()
@@ -440,7 +446,7 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier) -> dict:
+def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status) -> dict:
     """N > 1: config 4 (201088x2880 lm_head, rows split N ways, all-gather of the
     fp16 logits) and config 3 expert-parallel (128/N experts per GPU, all-reduce
     of y).  Times are the slowest rank's."""
@@ -473,7 +479,34 @@ def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier) -> dict:
         "rows_per_rank": hi - lo, "allgather_bytes_per_rank": (hi - lo) * 2,
         "gather": "fused (peer stores from the GEMV epilogue)" if comm.fused else "NCCL",
         "scaling": "strong"}
-    del t, ws
+    del t
+    status("detail_config4")
+
+    # config 4's batch-8 probe on the shards: fused gather (symmetric Y) and NCCL
+    B = 8
+    X = torch.stack([synth.activations(K, seed=20 + b) for b in range(B)])
+    forms = [("nccl", torch.empty((B, Mt), dtype=torch.float16, device="cuda"))]
+    if comm.fused:
+        forms.insert(0, ("fused", comm.alloc((B, Mt), torch.float16)))
+    b8 = {}
+    for name, Y in forms:
+        torch.cuda.synchronize()
+        barrier()
+        t = Timer(torch, lambda i, Y=Y: kb.gemm_int4_sharded(comm, ws[i % ncopy]["W"],
+                                                             ws[i % ncopy]["SB"], X, Y, B, P), 100)
+        t.build(100)
+        barrier()
+        t.run(100)
+        steps = 1000
+        dt = slowest(t.time(steps, barrier))
+        b8[name] = {"us_per_call": round(dt / steps * 1e6, 3),
+                    "tokens_per_s": round(B * steps / dt, 1),
+                    "weight_gbs_aggregate": round(nb * steps / dt / 1e9, 1)}
+        del t
+        status(f"detail_config4_batch8_{name}")
+    d["config4_lmhead_batch8"] = dict(b8, B=B, rows_per_rank=hi - lo,
+                                      allgather_bytes_per_rank=B * (hi - lo) * 2)
+    del ws
 
     Pm = kb.moe_params(2880, 2880, 128, 4)
     e_lo, e_hi = kb.expert_range(128, world, rank)

@@ -413,6 +413,15 @@ int graft_comm_status(graft_comm_t comm);
 int graft_gemv_int4_sharded(graft_comm_t comm, const void* W, const void* SB, const void* x,
                             void* y_full, const GraftGemvParams* P, graft_stream_t stream);
 
+/* The same for B = 1..16 tokens (graft_gemm_int4_sb_f16 on the shard): X fp16
+ * [B][K]; Y_full fp16 [B][nranks*M], row b the whole output of token b.  The
+ * rank's rows of every token land at Y_full + b*nranks*M + rank*M; fused
+ * (peer stores in the kernel's epilogue) with Y_full from graft_comm_alloc,
+ * else B in-place NCCL all-gathers in one group. */
+int graft_gemm_int4_sharded(graft_comm_t comm, const void* W, const void* SB, const void* X,
+                            void* Y_full, uint32_t B, const GraftGemvParams* P,
+                            graft_stream_t stream);
+
 /* Expert-parallel MoE block: the ranks split the n_experts experts into equal
  * contiguous ranges (rank r holds [r*E/n, (r+1)*E/n), `pool` holding just
  * those); the router runs on every rank, each rank computes its selected

@@ -23,7 +23,7 @@ from ._lib import (ExpertParams, ExpertScratch, GemvParams, GraftError, MoEForma
 __all__ = [
     "GemvParams", "VQParams", "MoEParams", "MoEFormat", "MoEScratch", "GraftError",
     "load", "version", "gemv_params", "xsum32", "gemv_int4_wide_unroll", "gemv_int4_fused",
-    "gemv_int4_simd", "gemv_int4_sb_f16out", "gemm_int4_sb_f16", "stream_read", "set_gemv_engine", "get_gemv_engine",
+    "gemv_int4_simd", "gemv_int4_sb_f16out", "gemm_int4_sb_f16", "gemm_int4_sharded", "stream_read", "set_gemv_engine", "get_gemv_engine",
     "device_errors",
     "ENGINE_TENSOR", "ENGINE_CUDA_CORE", "expert_params", "xsum32_f32", "gemv_int4_bf16",
     "ExpertScratchBuffers", "expert_forward", "ExpertStream", "vq_params", "gemv_vq_wide",
@@ -378,6 +378,13 @@ def gemv_int4_sharded(comm: Comm, W, SB, x, y_full, P: GemvParams, stream=None) 
     """This rank's row shard (P: its M rows) into y_full[rank*M:], then all-gather."""
     call("graft_gemv_int4_sharded", comm.handle, _p(W), _p(SB), _p(x), _p(y_full), C.byref(P),
          _s(stream))
+
+
+def gemm_int4_sharded(comm: Comm, W, SB, X, Y_full, B: int, P: GemvParams, stream=None) -> None:
+    """B tokens through this rank's row shard (P: its M rows), all-gathered so
+    that Y_full [B, nranks*M] holds every token's whole output."""
+    call("graft_gemm_int4_sharded", comm.handle, _p(W), _p(SB), _p(X), _p(Y_full), B,
+         C.byref(P), _s(stream))
 
 
 def moe_block_ep(comm: Comm, pool, R, x, y, P: MoEParams, fmt: MoEFormat | None,

@@ -82,6 +82,57 @@ __device__ __forceinline__ void wait_flags(const uint32_t* flags, int n, int sel
     }
 }
 
+// Waits (bounded) until cnt[p] >= need for every peer, then takes `need` back
+// off: a peer's next call adds only after this rank has entered that call.
+__device__ __forceinline__ void wait_flags_count(uint32_t* cnt, int n, int self, uint32_t need,
+                                                 unsigned* err, unsigned bit) {
+    const uint64_t t0 = global_ns();
+    for (int p = 0; p < n; ++p) {
+        if (p == self) continue;
+        while (ld_acquire_sys(cnt + p) < need) {
+            if (global_ns() - t0 > kPeerWaitNs) {
+                atomicOr(err, bit);
+                break;
+            }
+            __nanosleep(64);
+        }
+        atomicSub_system(cnt + p, need);
+    }
+}
+
+// The fused all-gather's handshake, in a kernel whose CTAs each store their
+// rows into every rank's copy of a symmetric buffer (call E = epoch + 1,
+// read after the dependency wait; block 0 has told each peer it entered E):
+//   gather_wait_entry  thread 0 waits until every peer has entered call E,
+//                      so its buffer may be written (the CTA syncs after);
+//   gather_publish     after a barrier that follows the CTA's peer stores:
+//                      one release add per peer, and the grid's last CTA
+//                      waits for every peer's CTAs and closes call E.
+__device__ __forceinline__ uint32_t gather_enter(const P2PGather* g) {
+    const uint32_t E = *reinterpret_cast<volatile uint32_t*>(g->epoch) + 1;
+    if (blockIdx.x == 0 && threadIdx.x < g->nranks && (int)threadIdx.x != g->rank)
+        st_release_sys(g->peer_entry[threadIdx.x] + g->rank, E);
+    return E;
+}
+__device__ __forceinline__ void gather_wait_entry(const P2PGather* g, uint32_t E) {
+    if (threadIdx.x == 0) wait_flags(g->entry, g->nranks, g->rank, E, g->err, 1u);
+}
+__device__ __forceinline__ void gather_publish(const P2PGather* g, uint32_t E) {
+    // the caller's barrier orders the CTA's stores before the release add
+    // (release is cumulative over what the thread observed)
+    if ((int)threadIdx.x < g->nranks && (int)threadIdx.x != g->rank)
+        red_release_sys(g->peer_cnt[threadIdx.x] + g->rank, 1u);
+    if (threadIdx.x == 0) {
+        const uint32_t t = atomicAdd(g->done_count, 1u);
+        if (t == gridDim.x - 1) {
+            // the last CTA here: every peer's CTAs have published into this buffer
+            wait_flags_count(g->cnt, g->nranks, g->rank, gridDim.x, g->err, 2u);
+            *g->done_count = 0;
+            *reinterpret_cast<volatile uint32_t*>(g->epoch) = E;
+        }
+    }
+}
+
 }  // namespace dev
 
 // Launches the int4 GEMV (interleaved SB, fp16 y) whose epilogue stores this
@@ -90,5 +141,12 @@ __device__ __forceinline__ void wait_flags(const uint32_t* flags, int n, int sel
 // the shape is not one the tile engine takes.
 int int4_gemv_gather(const void* W, const void* SB, const void* x, void* y_local, long y_off,
                      const GraftGemvParams* P, const P2PGather* g, cudaStream_t st);
+
+// The batched int4 GEMV (B tokens, int4_batch.cu) writing rows of Y with row
+// stride ldY; with g, its epilogue also stores each CTA's rows of every token
+// into every rank's copy at element offset y_off + b*ldY and completes the
+// gather.  Several launches when the tokens do not fit one.
+int int4_gemm_batch(const void* W, const void* SB, const void* X, void* Y, long ldY, uint32_t B,
+                    const GraftGemvParams* P, const P2PGather* g, long y_off, cudaStream_t st);
 
 }  // namespace graft

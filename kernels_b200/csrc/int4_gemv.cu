@@ -96,24 +96,6 @@ struct GemvArgs {
     const uint16_t* BI;        // bf16 per-row output bias added to y, or null
 };
 
-// Waits (bounded) until cnt[p] >= need for every peer, then takes `need` back
-// off: a peer's next call adds only after this rank has entered that call.
-__device__ __forceinline__ void wait_flags_count(uint32_t* cnt, int n, int self, uint32_t need,
-                                                 unsigned* err, unsigned bit) {
-    const uint64_t t0 = global_ns();
-    for (int p = 0; p < n; ++p) {
-        if (p == self) continue;
-        while (ld_acquire_sys(cnt + p) < need) {
-            if (global_ns() - t0 > kPeerWaitNs) {
-                atomicOr(err, bit);
-                break;
-            }
-            __nanosleep(64);
-        }
-        atomicSub_system(cnt + p, need);
-    }
-}
-
 // Fused all-gather epilogue: rows [r0, r1) (part sums in `cells`) as fp16
 // into every rank's copy of the symmetric output at y_off + r0, then the
 // completion handshake (graft_p2p.cuh).  ybuf: r1 - r0 halves of smem.
@@ -126,8 +108,7 @@ __device__ __forceinline__ void gather_rows(const P2PGather* g, const float* cel
         for (int q = 0; q < parts; ++q) v += cells[i * parts + q];
         ybuf[i] = __float2half_rn(v);
     }
-    // the peers must have entered this call before their buffers are written
-    if (threadIdx.x == 0) wait_flags(g->entry, g->nranks, g->rank, E, g->err, 1u);
+    gather_wait_entry(g, E);
     __syncthreads();
     const long o = y_off + r0;
     const bool vec = (o & 7) == 0 && (n & 7) == 0;
@@ -140,20 +121,8 @@ __device__ __forceinline__ void gather_rows(const P2PGather* g, const float* cel
             for (int i = threadIdx.x; i < n; i += nthreads) dst[i] = ybuf[i];
         }
     }
-    // publish this CTA's stores to each peer: the barrier orders them before
-    // the release add (release is cumulative over what the thread observed)
     __syncthreads();
-    if ((int)threadIdx.x < g->nranks && (int)threadIdx.x != g->rank)
-        red_release_sys(g->peer_cnt[threadIdx.x] + g->rank, 1u);
-    if (threadIdx.x == 0) {
-        const uint32_t t = atomicAdd(g->done_count, 1u);
-        if (t == gridDim.x - 1) {
-            // the last CTA here: every peer's CTAs have published into this buffer
-            wait_flags_count(g->cnt, g->nranks, g->rank, gridDim.x, g->err, 2u);
-            *g->done_count = 0;
-            *reinterpret_cast<volatile uint32_t*>(g->epoch) = E;
-        }
-    }
+    gather_publish(g, E);
 }
 
 // Shared memory: barriers, then (1024-aligned) the code ring, the scale
@@ -262,10 +231,7 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
     }
     pdl_wait();   // x, and the y this grid writes, may belong to the previous kernel
     // fused gather: this call's epoch; tell the peers this rank may be written to
-    const uint32_t E = a.gather ? *reinterpret_cast<volatile uint32_t*>(a.gather->epoch) + 1 : 0u;
-    if (a.gather && blockIdx.x == 0 && threadIdx.x < a.gather->nranks &&
-        (int)threadIdx.x != a.gather->rank)
-        st_release_sys(a.gather->peer_entry[threadIdx.x] + a.gather->rank, E);
+    const uint32_t E = a.gather ? gather_enter(a.gather) : 0u;
     XStage<WPG> xst;
     xst.load(a.x, a.K, a.x32);
     for (int i = 1; i < kDepth && i < mine; ++i) {

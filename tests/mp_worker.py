@@ -59,6 +59,29 @@ def main() -> int:
         print(f"rank {rank}: fused sharded gemv (4th call) max|d|/max|ref| = {rel3:.2e}", flush=True)
         ok &= bool(np.isfinite(got3).all()) and rel3 <= 2e-3
 
+        # B tokens through the row shards (config 4's batch probe): NCCL, then fused
+        for B, fused in ((8, False), (8, True), (12, True)):
+            X = torch.stack([synth.activations(K, seed=60 + b, device="cpu") for b in range(B)]).cuda()
+            if fused:
+                Y = comm.alloc((B, Mt), torch.float16)
+                Y.fill_(float("nan"))
+                for _ in range(3):      # back to back: epochs advance in lockstep
+                    kb.gemm_int4_sharded(comm, W, SB, X, Y, B, kb.gemv_params(hi - lo, K, G))
+            else:
+                Y = torch.full((B, Mt), float("nan"), dtype=torch.float16, device="cuda")
+                kb.gemm_int4_sharded(comm, W, SB, X, Y, B, kb.gemv_params(hi - lo, K, G))
+            torch.cuda.synchronize()
+            comm.status()
+            got = Y.cpu().numpy().astype(np.float64)
+            worst = 0.0
+            for b in range(B):
+                rb = oracle.gemv_int4_sb(full["W"].numpy().view(np.uint32), full["SB"].numpy(),
+                                         X[b].cpu().numpy(), G)
+                worst = max(worst, float(np.max(np.abs(got[b] - rb)) / np.max(np.abs(rb))))
+            print(f"rank {rank}: sharded gemm B={B} {'fused' if fused else 'nccl'} "
+                  f"max|d|/max|ref| = {worst:.2e}", flush=True)
+            ok &= bool(np.isfinite(got).all()) and worst <= 2e-3
+
         # expert-parallel MoE: rank r's pool holds experts [r*E/n, (r+1)*E/n)
         P = kb.moe_params(2880, 2880, 16 * world, 4)
         e_lo, e_hi = kb.expert_range(P.n_experts, world, rank)

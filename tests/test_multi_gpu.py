@@ -1,4 +1,4 @@
-"""GPU, 2+ GPUs: graft_gemv_int4_sharded and graft_moe_block_ep through the C
+"""GPU, 2+ GPUs: graft_gemv_int4_sharded, graft_gemm_int4_sharded and graft_moe_block_ep through the C
 ABI against the oracle, as torchrun ranks (tests/mp_worker.py).  Skipped on a
 single-GPU box."""
 from __future__ import annotations
