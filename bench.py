@@ -150,12 +150,14 @@ class Timer:
         self.torch.cuda.synchronize()
 
     def run(self, steps: int) -> None:
+        # every replay and every first-call set-up on the timer's own stream:
+        # a fused multi-GPU call must never overlap another on the same GPU
         done = 0
-        while done < steps:
-            n = min(self.chunk, steps - done)
-            n = n if n == self.chunk else n
-            self._graph(n, done).replay()
-            done += n
+        with self.torch.cuda.stream(self.stream):
+            while done < steps:
+                n = min(self.chunk, steps - done)
+                self._graph(n, done).replay()
+                done += n
 
     def time(self, steps: int, barrier=None) -> float:
         """Seconds for exactly `steps` steps (device time)."""
@@ -171,8 +173,7 @@ class Timer:
             barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(self.stream)
-        with torch.cuda.stream(self.stream):
-            self.run(steps)
+        self.run(steps)
         e1.record(self.stream)
         torch.cuda.synchronize()
         if barrier:
