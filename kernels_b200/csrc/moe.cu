@@ -1189,8 +1189,8 @@ int graft_moe_block(const void* pool, const float* R, const float* x, float* y,
 // resident-expert list, fp16 x, h, sum(h)) lives in the fixed device array
 // below instead of in a buffer the caller allocates.  It is for callers that
 // cannot call cudaMalloc: hosts that own every byte of device memory through
-// their own arena and give a library no allocator, hosts that must not
-// allocate after start-up, and code that runs while a stream is being captured.
+// their own arena and give a library no allocator, and hosts that must not
+// allocate after start-up.
 //
 // Limits: the array holds kNoAllocScratchBytes (256 KiB) per device, enough for
 // hidden = inter = 2880 at top_k = 8 (the gpt-oss-120b block needs ~31 KiB at

@@ -1,7 +1,7 @@
 """GPU: graft_moe_block_noalloc, the MoE block for callers that cannot call
 cudaMalloc (hosts that own all device memory and give a library no allocator,
-hosts that must not allocate after start-up, code running during stream
-capture).  It keeps its scratch in a fixed array inside the library; these
+hosts that must not allocate after start-up).  It keeps its scratch in a fixed
+array inside the library; these
 tests call it through the C ABI and check it against graft_moe_block_ex with a
 caller-provided workspace, twice in a row with different tokens, so that the
 second call cannot pass on the first call's leftovers.
