@@ -651,20 +651,22 @@ def measure_per_shape(torch, kb, sets, xs, ys, Ps) -> dict:
     return res
 
 
-def measure_vq(torch, kb, synth, timer_cls) -> dict:
-    """VQ config 2 (one fp16 scale per row, fp16 y), 8 rotating copies."""
+def measure_vq(torch, kb, synth, timer_cls, scale_group=None) -> dict:
+    """VQ config 2 (one fp16 scale per row, fp16 y), 8 rotating copies; with
+    scale_group=32, the reference's own per-32 scales (the quantiser's output)."""
     vq = {}
     for M, K in [(4096, 4096), (14336, 4096)]:
-        ws = [synth.vq_weights(M, K, seed=c) for c in range(NCOPY)]
+        sg = scale_group or K
+        ws = [synth.vq_weights(M, K, seed=c, scale_group=sg) for c in range(NCOPY)]
         x = synth.activations(K, seed=5)
         y = torch.empty(M, dtype=torch.float16, device="cuda")
         P = kb.vq_params(M, K)
         t = timer_cls(torch, lambda i: kb.gemv_vq_ex(ws[i % NCOPY]["IDX"], ws[i % NCOPY]["C"],
-                                                     ws[i % NCOPY]["S"], K, x, y, P), 400)
+                                                     ws[i % NCOPY]["S"], sg, x, y, P), 400)
         t.run(400)
         steps = 4000
         dt = t.time(steps)
-        nb = M * K // 2 + 2 * M + 1024 + 2 * K + 2 * M
+        nb = M * K // 2 + 2 * M * (K // sg) + 1024 + 2 * K + 2 * M
         vq[f"{M}x{K}"] = {"us": round(dt / steps * 1e6, 3), "gbs": round(nb * steps / dt / 1e9, 1)}
         del ws
     return vq
@@ -814,6 +816,7 @@ def measure_detail(torch, kb, synth, timer_cls) -> dict:
     del bufs
 
     d["vq_config2"] = measure_vq(torch, kb, synth, timer_cls)
+    d["vq_per32_scales"] = measure_vq(torch, kb, synth, timer_cls, scale_group=32)
     d["expert_stream"] = measure_expert_stream(torch, kb, synth)
     d["batched_gemv"] = measure_batch(torch, kb, synth, timer_cls)
     d["vq_quantize"] = measure_vq_quantize(torch, kb)
