@@ -69,6 +69,92 @@ def profile_traffic() -> float | None:
     return None
 
 
+# ----------------------------------------------------------------- parity --
+# Output checks against the CPU oracle (the reference's fp64 CPU references,
+# oracle/), run once per phase OUTSIDE every timed region: the checker, not
+# the thing measured.
+PARITY_TOL = 1e-3
+# per element (outputs >= 1e-2 of the largest): the reference's own 2e-3
+# (int4-gemv/src/main.mm:476); fp16 output rounding (2^-11 of the element) and
+# the decode's fp32 partial sums at ~1024x the signal sit between 1e-3 and it
+PARITY_TOL_ELEM = 2e-3
+
+
+def parity_metrics(got, ref) -> dict:
+    """max|got - ref| / max|ref| (the reference's own acceptance metric,
+    int4-gemv/src/main.mm:472-476) and the largest per-element relative error
+    over the outputs with |ref| >= 1e-2 * max|ref|."""
+    import numpy as np
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    m = max(float(np.max(np.abs(ref))), 1e-30)
+    d = np.abs(got - ref)
+    keep = np.abs(ref) >= 1e-2 * m
+    return {"max_rel": float(np.max(d) / m),
+            "elem_rel": float(np.max(d[keep] / np.abs(ref[keep]))) if keep.any() else 0.0,
+            "finite": bool(np.isfinite(got).all())}
+
+
+def worst(a: dict | None, b: dict) -> dict:
+    if a is None:
+        return dict(b)
+    out = dict(a)
+    for k, v in b.items():
+        if isinstance(v, bool):
+            out[k] = bool(out.get(k, True)) and v
+        elif isinstance(v, (int, float)):
+            out[k] = max(out.get(k, 0.0), v)
+    return out
+
+
+def passed(m: dict) -> bool:
+    """max_rel within the tolerance (the reference's own metric), and for the
+    GEMV phases elem_rel within PARITY_TOL_ELEM.  The
+    MoE block keeps h in fp16 as the reference's kernels do while the fp64
+    oracle does not round it, so its per-element figure is reported only."""
+    elem_ok = m.get("elem_rel", 0.0) <= PARITY_TOL_ELEM or "topk_exact" in m
+    return (m.get("finite", True) and m.get("max_rel", 0.0) <= PARITY_TOL and elem_ok
+            and m.get("replicas_identical", True) and m.get("topk_exact", True))
+
+
+def check_rows(W, SB, x, y_rows, stride: int, nthreads: int) -> dict:
+    """The fp16 outputs y_rows of W (every `stride`-th row) against the oracle."""
+    import numpy as np
+    import oracle
+    Wn = W[::stride].contiguous().cpu().numpy().view(np.uint32)
+    SBn = SB[::stride].contiguous().cpu().numpy().view(np.uint16)
+    ref = oracle.gemv_int4_sb(Wn, SBn, x.contiguous().cpu().numpy().view(np.uint16), GROUP,
+                              nthreads)
+    return parity_metrics(y_rows[::stride].float().cpu().numpy(), ref)
+
+
+def replicas_identical(torch, dist, buf, world: int) -> bool:
+    """Every rank's copy of a gathered or reduced output is bit-identical
+    (collective: every rank calls it)."""
+    if dist is None or world == 1:
+        return True
+    t = buf.contiguous().view(torch.uint8).reshape(-1)   # bytes: NCCL takes uint8
+    got = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(got, t)
+    torch.cuda.synchronize()
+    return all(bool(torch.equal(g, t)) for g in got)
+
+
+def worst_over_ranks(dist, world: int, m: dict) -> dict:
+    if dist is None or world == 1:
+        return m
+    got = [None] * world
+    dist.all_gather_object(got, m)
+    out = None
+    for g in got:
+        out = worst(out, g)
+    return out
+
+
+def oracle_threads(world: int) -> int:
+    return max(1, (os.cpu_count() or 1) // max(1, world))
+
+
 # ----------------------------------------------------------------- clocks --
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons, sampled while the timed region runs."""
@@ -159,8 +245,11 @@ class Timer:
                 self._graph(n, done).replay()
                 done += n
 
-    def time(self, steps: int, barrier=None) -> float:
-        """Seconds for exactly `steps` steps (device time)."""
+    def time(self, steps: int, barrier=None, sync_first: bool = True) -> float:
+        """Seconds for exactly `steps` steps (device time).  With sync_first
+        false the timed replays queue right behind the work already on the
+        timer's stream (the warm-up), so the GPU does not idle in between; the
+        events still bracket exactly the timed replays."""
         torch = self.torch
         # build every graph the timed region replays before timing starts
         done = 0
@@ -168,9 +257,10 @@ class Timer:
             n = min(self.chunk, steps - done)
             self._graph(n, done)
             done += n
-        torch.cuda.synchronize()
-        if barrier:
-            barrier()
+        if sync_first:
+            torch.cuda.synchronize()
+            if barrier:
+                barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(self.stream)
         self.run(steps)
@@ -179,6 +269,24 @@ class Timer:
         if barrier:
             barrier()
         return e0.elapsed_time(e1) / 1e3
+
+
+def settle(torch, timer: Timer, dist, seconds: float) -> int:
+    """Replays the timer's step for about `seconds` of wall time (the same
+    number of steps on every rank), then synchronises; returns the steps."""
+    timer.run(timer.chunk)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    timer.run(timer.chunk)
+    torch.cuda.synchronize()
+    per = max(1e-6, time.perf_counter() - t0)
+    n = max(1, int(seconds / per)) * timer.chunk
+    if dist is not None:
+        t = torch.tensor([n], dtype=torch.int64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        n = int(t.item())
+    timer.run(n)
+    return n + 2 * timer.chunk
 
 
 # --------------------------------------------------------------- workloads --
@@ -197,7 +305,12 @@ def build_sweep(torch, kb, synth, shapes, seed_base: int):
 
 
 def run_reference_arm(args) -> None:
-    """The reference's own CPU cpuRef on a row sample of each sweep shape."""
+    """The reference's own CPU cpuRef (int4-gemv/src/main.mm:64-92, compiled from
+    the reference sources into oracle/_ref) over the whole config-1 sweep: every
+    row of the four shapes per step, fp64, std::thread x hardware_concurrency, as
+    the reference runs it before timing its kernels.  If K + W full steps would
+    not end within about two minutes, each step runs a contiguous row block of
+    every shape instead (reported as such)."""
     import numpy as np
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -209,75 +322,109 @@ def run_reference_arm(args) -> None:
                           "reference CPU routines (oracle/_ref/libref.so) were not built"}))
         return
     rng = np.random.default_rng(0)
-    stride = 1024                    # every 1024th row of each shape: a bounded sample
-    data = []
+    full = []
     for M, K in SWEEP:
-        m = (M + stride - 1) // stride
-        W = rng.integers(0, 2**32, size=(m, K // 8), dtype=np.uint64).astype(np.uint32)
-        S = np.abs(rng.normal(0, 0.02, (m, K // GROUP))).astype(np.float16)
+        W = rng.integers(0, 2**32, size=(M, K // 8), dtype=np.uint32)
+        S = np.abs(rng.normal(0, 0.02, (M, K // GROUP))).astype(np.float16)
         B = (S.astype(np.float32) * -8).astype(np.float16)
         x = rng.normal(0, 1, K).astype(np.float16)
-        data.append((W, S, B, x, np.empty(m, np.float32), m, K))
-    bytes_step = sweep_bytes([(d[5], d[6]) for d in data])
+        full.append((W, S, B, x, np.empty(M, np.float32), M, K))
 
-    def step():
+    def run(data):
         for W, S, B, x, y, m, K in data:
             L.ref_int4_cpuRef(W.ctypes.data, S.ctypes.data, B.ctypes.data, x.ctypes.data,
                               y.ctypes.data, m, K, GROUP)
 
-    for _ in range(args.warmup):
-        step()
+    t0 = time.perf_counter()
+    run(full)                                    # first warm-up step, timed to size the run
+    t_full = time.perf_counter() - t0
+    budget = 120.0
+    frac = min(1.0, budget / max(1e-9, t_full * (args.steps + args.warmup)))
+    if frac < 1.0:   # contiguous row blocks (out of cache, like the full matrices)
+        data = [(W[:max(16, int(M * frac))], S[:max(16, int(M * frac))],
+                 B[:max(16, int(M * frac))], x, y, max(16, int(M * frac)), K)
+                for W, S, B, x, y, M, K in full]
+    else:
+        data = full
+    bytes_step = sweep_bytes([(d[5], d[6]) for d in data])
+    for _ in range(args.warmup - 1):
+        run(data)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        run(data)
     dt = time.perf_counter() - t0
     cores = os.cpu_count() or 1
     v = bytes_step * args.steps / dt / 1e9
+    same = frac >= 1.0
     print(json.dumps({
         "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "config1_int4_sweep_rowsample", "row_sample": f"1/{stride}",
-                   "shapes": [f"{M}x{K}" for M, K in SWEEP], "group": GROUP},
+        "config": {"workload": "config1_int4_sweep_batch1",
+                   "shapes": [f"{M}x{K}" for M, K in SWEEP], "group": GROUP,
+                   "bytes_per_step": bytes_step,
+                   "rows": "all" if same else f"first {frac:.4f} of every shape's rows"},
+        "same_config": same,
         "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores,
                          "kind": "reference",
-                         "sample": f"every {stride}th row of each config-1 shape per step; "
-                                   "cpuRef (fp64, std::thread x hardware_concurrency)"},
+                         "sample": ("every row of the four config-1 shapes per step"
+                                    if same else f"rows [0, {frac:.4f}*M) of every shape per "
+                                    "step") + "; cpuRef (fp64, std::thread x "
+                                    "hardware_concurrency)"},
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }))
 
 
 def cpu_baseline_leg() -> dict:
-    """Reference cpuRef on a bounded sample, rank 0 at N=1 (about 10-20 s)."""
+    """CPU baselines on the GPU box's host cores, rank 0 at N=1 (about 10-20 s):
+    the reference's own cpuRef (fp64, all host threads) and the fp32 fast path
+    (oracle/cpu_fast.cpp, the reference's cpu_gemv_neon restated portably,
+    hetero-gemv/src/cpu_gemv.h:88-103), each on the lm_head shape's first 1/16
+    of rows (contiguous, far beyond the CPU caches)."""
     import numpy as np
     import oracle
     L = oracle.ref_lib()
     rng = np.random.default_rng(1)
-    M, K = 128256 // 16, 4096                     # 1/16 of the lm_head rows
-    W = rng.integers(0, 2**32, size=(M, K // 8), dtype=np.uint64).astype(np.uint32)
+    M, K = 128256 // 16, 4096
+    W = rng.integers(0, 2**32, size=(M, K // 8), dtype=np.uint32)
     S = np.abs(rng.normal(0, 0.02, (M, K // GROUP))).astype(np.float16)
     B = (S.astype(np.float32) * -8).astype(np.float16)
     x = rng.normal(0, 1, K).astype(np.float16)
+    SB = np.ascontiguousarray(np.stack([S, B], -1))
     nbytes = sweep_bytes([(M, K)])
+
+    def timed(f, seconds):
+        f()
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds and reps < 400:
+            f()
+            reps += 1
+        return (time.perf_counter() - t0) / reps, reps
+
     if L is not None:
         y = np.empty(M, np.float32)
         f = lambda: L.ref_int4_cpuRef(W.ctypes.data, S.ctypes.data, B.ctypes.data,  # noqa
                                       x.ctypes.data, y.ctypes.data, M, K, GROUP)
         kind, desc = "reference", "cpuRef (fp64, all host threads)"
     else:
-        SB = np.stack([S, B], -1)
         f = lambda: oracle.gemv_int4_sb(W, SB, x, GROUP)  # noqa
         kind, desc = "port", "oracle restatement (fp64, all host threads)"
-    f()
-    reps, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < 8.0 and reps < 200:
-        f()
-        reps += 1
-    dt = (time.perf_counter() - t0) / reps
+    dt, reps = timed(f, 8.0)
+    threads = [0]
+
+    def fast():
+        threads[0] = oracle.cpu_fast_gemv_int4_sb(W, SB, x, GROUP)[1]
+
+    dt_fast, reps_fast = timed(fast, 6.0)
     return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count() or 1,
-            "kind": kind, "sample": f"{M}x{K} rows (1/16 of lm_head), {reps} calls; {desc}"}
+            "kind": kind, "sample": f"{M}x{K} rows (1/16 of lm_head), {reps} calls; {desc}",
+            "fast_fp32": {"value": round(nbytes / dt_fast / 1e9, 3), "unit": "GB/s",
+                          "cores": threads[0], "kind": "port",
+                          "sample": f"{M}x{K}, {reps_fast} calls; oracle/cpu_fast.cpp, fp32 "
+                                    "restatement of cpu_gemv_neon "
+                                    "(hetero-gemv/src/cpu_gemv.h:88-103)"}}
 
 
 def main() -> None:
@@ -356,18 +503,22 @@ def main() -> None:
 
     chunk = 200
     timer = Timer(torch, step, chunk)
-    timer.build(args.warmup)   # capture first: ranks then start replaying together
-    barrier()
-    timer.run(args.warmup)
-    torch.cuda.synchronize()
+    for n in (args.warmup, args.steps, chunk):   # capture first: ranks then replay together
+        timer.build(n)
     uuid = None
     try:
         uuid = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
     except Exception:
         pass
     sampler = ClockSampler(uuid)
-    time.sleep(0.3)
-    dt = timer.time(args.steps, barrier)
+    time.sleep(0.3)            # nvidia-smi's first sample
+    barrier()
+    # Clock settle, as the reference's harness settles the clocks under load
+    # before it measures (int4-gemv/src/main.mm:266-292): the step itself,
+    # replayed for about 0.1 s, so the timed steps do not start from an idle GPU.
+    settle_steps = settle(torch, timer, dist, seconds=0.1)
+    timer.run(args.warmup)
+    dt = timer.time(args.steps, barrier, sync_first=dist is not None)
     clocks = sampler.stop()
     if dist is not None:
         t = torch.tensor([dt], dtype=torch.float64, device="cuda")
@@ -377,6 +528,11 @@ def main() -> None:
     comm_status = {}
     if comm is not None:
         status_all("sweep")
+    parity = {"tol": PARITY_TOL}
+    parity["sweep"] = verify_sweep(torch, kb, sets, xs, ys, Ps, comm, gathered, world, rank,
+                                   dist)
+    if comm is not None:
+        status_all("sweep_parity")
     gpu_launches = len(SWEEP) * args.steps
 
     # roofline of the dominant kernel: the same launches, achieved = bytes / time
@@ -393,7 +549,7 @@ def main() -> None:
     e2e = measure_e2e(torch, kb, sets, xs, Ps, steps=min(args.steps, 3000), comm=comm,
                       world=world, dist=dist, barrier=barrier)
     if not args.no_detail and world == 1:
-        detail = measure_detail(torch, kb, synth, timer_cls=Timer)
+        detail = measure_detail(torch, kb, synth, timer_cls=Timer, parity=parity)
         detail["sweep_per_shape"] = measure_per_shape(torch, kb, sets, xs, ys, Ps)
         # the same shapes on the CUDA-core engine (no tensor cores), for comparison
         kb.set_gemv_engine("cuda-core")
@@ -410,7 +566,8 @@ def main() -> None:
         status_all("e2e")
     if not args.no_detail and world > 1:
         del sets
-        detail = measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status_all)
+        detail = measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status_all,
+                               parity)
         status_all("detail_moe_ep")
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
@@ -432,8 +589,12 @@ def main() -> None:
                                        + ("fused into the GEMV over NVLink peer stores)"
                                           if comm is not None and comm.fused else "NCCL)")
                                        if world > 1 else "single"),
-                       "timing": f"CUDA events around CUDA-graph replays ({chunk} steps/graph)"},
+                       "timing": f"CUDA events around CUDA-graph replays ({chunk} steps/graph), "
+                                 f"after a clock settle of {settle_steps} untimed steps under "
+                                 "load and the warm-up"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+            "parity": parity,
+            "parity_ok": all(passed(v) for k, v in parity.items() if isinstance(v, dict)),
             "gpu_launches": gpu_launches, "detail": detail,
         }
         if comm is not None:
@@ -447,7 +608,32 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status) -> dict:
+def verify_sweep(torch, kb, sets, xs, ys, Ps, comm, gathered, world, rank, dist) -> dict:
+    """One step of the headline sweep (weight copy 0) against the oracle: each
+    rank checks its own rows of every shape (every 4th row); at N > 1 the rows
+    are read from the rank's copy of the gathered output, and every rank's copy
+    of it must be bit-identical, so every rank holds the whole checked output."""
+    torch.cuda.synchronize()
+    m, same = None, True
+    for si, ((W, SB), x, P) in enumerate(zip(sets[0], xs, Ps)):
+        if comm is None:
+            ys[si].fill_(float("nan"))
+            kb.gemv_int4_sb_f16out(W, SB, x, ys[si], P)
+            mine = ys[si]
+        else:
+            kb.gemv_int4_sharded(comm, W, SB, x, gathered[si], P)
+            mine = gathered[si][rank * P.M:(rank + 1) * P.M]
+        torch.cuda.synchronize()
+        m = worst(m, check_rows(W, SB, x, mine, 4, oracle_threads(world)))
+        if comm is not None:
+            same &= replicas_identical(torch, dist, gathered[si], world)
+    m["replicas_identical"] = same
+    m["rows_checked"] = "every 4th row of every shape, on every rank"
+    return worst_over_ranks(dist, world, m)
+
+
+def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status,
+                  parity: dict) -> dict:
     """N > 1: config 4 (201088x2880 lm_head, rows split N ways, all-gather of the
     fp16 logits) and config 3 expert-parallel (128/N experts per GPU, all-reduce
     of y).  Times are the slowest rank's."""
@@ -482,6 +668,14 @@ def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status) ->
         "scaling": "strong"}
     del t
     status("detail_config4")
+    # parity: one call on weight copy 0, each rank's rows (every 8th) against the oracle
+    torch.cuda.synchronize()
+    kb.gemv_int4_sharded(comm, ws[0]["W"], ws[0]["SB"], x, yf, P)
+    torch.cuda.synchronize()
+    pm = check_rows(ws[0]["W"], ws[0]["SB"], x, yf[lo:hi], 8, oracle_threads(world))
+    pm["replicas_identical"] = replicas_identical(torch, dist, yf, world)
+    parity["config4_lmhead"] = worst_over_ranks(dist, world, pm)
+    status("detail_config4_parity")
 
     # config 4's batch-8 probe on the shards: fused gather (symmetric Y) and NCCL
     B = 8
@@ -505,6 +699,16 @@ def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status) ->
                     "weight_gbs_aggregate": round(nb * steps / dt / 1e9, 1)}
         del t
         status(f"detail_config4_batch8_{name}")
+        torch.cuda.synchronize()
+        kb.gemm_int4_sharded(comm, ws[0]["W"], ws[0]["SB"], X, Y, B, P)
+        torch.cuda.synchronize()
+        pm = None
+        for b in range(B):
+            pm = worst(pm, check_rows(ws[0]["W"], ws[0]["SB"], X[b], Y[b, lo:hi], 16,
+                                      oracle_threads(world)))
+        pm["replicas_identical"] = replicas_identical(torch, dist, Y, world)
+        parity[f"config4_batch8_{name}"] = worst_over_ranks(dist, world, pm)
+        status(f"detail_config4_batch8_{name}_parity")
     d["config4_lmhead_batch8"] = dict(b8, B=B, rows_per_rank=hi - lo,
                                       allgather_bytes_per_rank=B * (hi - lo) * 2)
     del ws
@@ -528,7 +732,37 @@ def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status) ->
     d["moe_config3_ep"] = {"us_per_token": round(dt / steps * 1e6, 3),
                            "experts_per_gpu": e_hi - e_lo, "allreduce": "fp32 y[2880]"}
     del t
+    status("detail_moe_ep")
+    # parity: one token; every rank's y must be bit-identical, and rank 0 checks
+    # it and the selected experts against the oracle over the whole pool
+    torch.cuda.synchronize()
+    y.fill_(float("nan"))
+    kb.moe_block_ep(comm, shard, R, xs_[0], y, Pm, fmt, wsp)
+    torch.cuda.synchronize()
+    same = replicas_identical(torch, dist, y, world)
+    pm = {}
+    if rank == 0:
+        pm = check_moe(torch, kb, synth, Pm, R, xs_[0], y, wsp)
+    pm["replicas_identical"] = same
+    parity["moe_config3_ep"] = worst_over_ranks(dist, world, pm)
     return d
+
+
+def check_moe(torch, kb, synth, P, R, x, y, ws) -> dict:
+    """The MoE block output y (and the selected experts) against the oracle
+    over the whole seeded config-3 pool (BASELINE format)."""
+    import numpy as np
+    import oracle
+    full, _ = synth.moe_pool(P, scale_f16=True, has_bias_out=False, act_f16=True, seed=0)
+    pool = full.cpu().numpy()
+    del full
+    cfg = oracle.moe_cfg(P, scale_bf16=False, has_bias_out=False, router_f16=True)
+    idx, _, _, _, yref = oracle.moe_block(cfg, pool, R.cpu().numpy().view(np.uint16),
+                                          x.cpu().numpy().view(np.uint16))
+    got_idx = ws.tensor("idx", torch.int32, P.top_k).cpu().numpy().view(np.uint32)
+    m = parity_metrics(y.float().cpu().numpy(), yref)
+    m["topk_exact"] = bool(np.array_equal(np.sort(got_idx), np.sort(idx)))
+    return m
 
 
 def measure_e2e(torch, kb, sets, xs, Ps, steps: int, comm=None, world=1, dist=None,
@@ -804,7 +1038,7 @@ def measure_vq_quantize(torch, kb) -> dict:
     return out
 
 
-def measure_detail(torch, kb, synth, timer_cls) -> dict:
+def measure_detail(torch, kb, synth, timer_cls, parity: dict | None = None) -> dict:
     d = {}
     # read-only ceiling over the same kind of rotation (8 x 1 GB)
     bufs = [torch.empty(1 << 30, dtype=torch.uint8, device="cuda") for _ in range(4)]
@@ -840,6 +1074,14 @@ def measure_detail(torch, kb, synth, timer_cls) -> dict:
                         "launches_per_token": 3,
                         "note": "16 rotating tokens; the experts they select (512 MB pool "
                                 "reads) mostly miss L2"}
+    del t
+    if parity is not None:
+        torch.cuda.synchronize()
+        y.fill_(float("nan"))
+        kb.moe_block_ex(pool, R, xs_[0], y, P, fmt, ws)
+        torch.cuda.synchronize()
+        del pool
+        parity["moe_config3"] = check_moe(torch, kb, synth, P, R, xs_[0], y, ws)
     return d
 
 

@@ -125,6 +125,7 @@ SIGNATURES: dict[str, tuple] = {
     "graft_comm_free": (INT, [P, P]),
     "graft_comm_fused": (INT, [P]),
     "graft_comm_status": (INT, [P]),
+    "graft_comm_set_wait_limit": (INT, [P, U64]),
     "graft_gemv_int4_sharded": (INT, [P, P, P, P, P, C.POINTER(GemvParams), P]),
     "graft_gemm_int4_sharded": (INT, [P, P, P, P, P, U32, C.POINTER(GemvParams), P]),
     "graft_moe_block_ep": (INT, [P, P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEFormat),

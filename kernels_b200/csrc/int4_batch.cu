@@ -419,11 +419,11 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemm_batch_kernel(
         const int r0 = kTileRows * T0, n = min(a.M, kTileRows * T1) - r0;
         __syncthreads();
         const uint32_t E = s_epoch;
-        gather_wait_entry(gp, E);
-        __syncthreads();
+        // false: a peer never entered this call -- its copy is not written
+        const bool peers = gather_wait_entry(gp, E);
         const bool vec = ((a.y_off + r0) & 7) == 0 && (a.ldY & 7) == 0 && (n & 7) == 0;
         for (int p = 0; p < gp->nranks; ++p) {
-            if (p == gp->rank) continue;
+            if (p == gp->rank || !peers) continue;
             for (int b = 0; b < a.B; ++b) {
                 const __half* src = a.Y + b * a.ldY + r0;
                 __half* dst = reinterpret_cast<__half*>(gp->buf[p]) + a.y_off + b * a.ldY + r0;
@@ -436,7 +436,7 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemm_batch_kernel(
             }
         }
         __syncthreads();
-        gather_publish(gp, E);
+        gather_publish(gp, E, peers);
     }
 }
 

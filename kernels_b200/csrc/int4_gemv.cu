@@ -108,11 +108,13 @@ __device__ __forceinline__ void gather_rows(const P2PGather* g, const float* cel
         for (int q = 0; q < parts; ++q) v += cells[i * parts + q];
         ybuf[i] = __float2half_rn(v);
     }
-    gather_wait_entry(g, E);
-    __syncthreads();
+    // false: a peer never entered this call -- write this rank's copy only
+    // (the barrier inside also makes ybuf visible to the whole CTA)
+    const bool peers = gather_wait_entry(g, E);
     const long o = y_off + r0;
     const bool vec = (o & 7) == 0 && (n & 7) == 0;
     for (int p = 0; p < g->nranks; ++p) {
+        if (!peers && p != g->rank) continue;
         __half* dst = reinterpret_cast<__half*>(g->buf[p]) + o;
         if (vec) {
             for (int i = threadIdx.x; i < n / 8; i += nthreads)
@@ -122,7 +124,7 @@ __device__ __forceinline__ void gather_rows(const P2PGather* g, const float* cel
         }
     }
     __syncthreads();
-    gather_publish(g, E);
+    gather_publish(g, E, peers);
 }
 
 // Shared memory: barriers, then (1024-aligned) the code ring, the scale
@@ -183,6 +185,7 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
         }
     };
     It iss{warp / a.parts, warp % a.parts}, cmp = iss;
+    const uint64_t pol = l2_evict_first();
     auto code_of = [&](int i) { return codes + (warp * kDepth + i) * PG::CODE_BYTES; };
     auto scale_of = [&](int i) { return scales + (warp * kDepth + i) * sslot; };
     auto bar_of = [&](int i) { return smem_u32(&bars[warp * kDepth + i]); };
@@ -207,18 +210,21 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
         if (a.map3) bytes += (uint32_t)(WPG - nseg) * kTileRows * 128;   // the full box
         mbar_arrive_expect_tx(bar, bytes);
         fence_proxy_async_smem();
+        // weights and scales are read once per call: evict them first from L2,
+        // so that x and the outputs stay cached across the stream
         if (a.map3) {
-            tma_load_3d(cd, &a.wmap, 0, row0, c0 / 8, bar);
+            tma_load_3d_hint(cd, &a.wmap, 0, row0, c0 / 8, bar, pol);
         } else {
             for (int sg = 0; sg < nseg; ++sg)
-                tma_load_2d(cd + sg * kTileRows * 128, &a.wmap, 4 * c0 + 32 * sg, row0, bar);
+                tma_load_2d_hint(cd + sg * kTileRows * 128, &a.wmap, 4 * c0 + 32 * sg, row0, bar,
+                                 pol);
         }
         if (a.scale_map) {
-            tma_load_2d(sd, &a.smap, g0, row0, bar);
-            if (SG::NARR == 2) tma_load_2d(sd + a.scap, &a.bmap, g0, row0, bar);
+            tma_load_2d_hint(sd, &a.smap, g0, row0, bar, pol);
+            if (SG::NARR == 2) tma_load_2d_hint(sd + a.scap, &a.bmap, g0, row0, bar, pol);
         } else {
-            bulk_copy(sc0, bar);
-            bulk_copy(sc1, bar);
+            bulk_copy_hint(sc0, bar, pol);
+            bulk_copy_hint(sc1, bar, pol);
         }
     };
 

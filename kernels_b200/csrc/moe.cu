@@ -477,21 +477,22 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_gate_up_mma(
 // until every peer's CTAs have published, sums the slots in rank order -- the
 // same order on every rank, so every rank gets the same bits -- into y and
 // closes call E.  The handshake is the fused gather's (graft_p2p.cuh).
-__device__ void ep_reduce_epilogue(const graft::P2PGather* g, uint32_t E, void* y, int y_f16,
-                                   int n) {
+__device__ void ep_reduce_epilogue(const graft::P2PGather* g, uint32_t E, bool wrote_peers,
+                                   void* y, int y_f16, int n) {
     using namespace graft::dev;
     __shared__ int s_last;
     __syncthreads();
-    if ((int)threadIdx.x < g->nranks && (int)threadIdx.x != g->rank)
+    if (wrote_peers && (int)threadIdx.x < g->nranks && (int)threadIdx.x != g->rank)
         red_release_sys(g->peer_cnt[threadIdx.x] + g->rank, 1u);
     if (threadIdx.x == 0) {
         __threadfence();
-        const uint32_t t = atomicAdd(g->done_count, 1u);
-        s_last = t == gridDim.x - 1;
-        if (s_last) wait_flags_count(g->cnt, g->nranks, g->rank, gridDim.x, g->err, 2u);
+        s_last = atomicAdd(g->done_count, 1u) == gridDim.x - 1;
     }
     __syncthreads();
     if (!s_last) return;
+    // the last CTA here: every peer's CTAs have published their slots
+    if (threadIdx.x < 32) warp_wait_counts(g, gridDim.x, 2u);
+    __syncthreads();
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     const float* slots = reinterpret_cast<const float*>(g->buf[g->rank]);
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -642,18 +643,17 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
         }
     cluster.sync();
     const int ns = tab->n;
-    if (a.red) {
-        // the peers must have entered this call before their buffers are written
-        graft::dev::gather_wait_entry(a.red, s_epoch);
-        __syncthreads();
-    }
+    // the peers must have entered this call before their buffers are written
+    // (false: one never did -- only this rank's slot copy is written)
+    const bool peers = a.red ? graft::dev::gather_wait_entry(a.red, s_epoch) : false;
     for (int q = p * NW * 32 + threadIdx.x; q < nt * kTileRows; q += ncl_cta * NW * 32) {
         float acc = 0.f;
         for (int e = 0; e < ns; ++e) acc += wgt[tab->j[e]] * cluster.map_shared_rank(ysl, e)[q];
         const int m = T0 * kTileRows + q;
         if (a.red) {
             for (int r = 0; r < a.red->nranks; ++r)
-                reinterpret_cast<float*>(a.red->buf[r])[(size_t)a.red->rank * graft::kReduceMaxFloats + m] = acc;
+                if (peers || r == a.red->rank)
+                    reinterpret_cast<float*>(a.red->buf[r])[(size_t)a.red->rank * graft::kReduceMaxFloats + m] = acc;
         } else if (a.y_f16) {
             reinterpret_cast<__half*>(y)[m] = __float2half_rn(acc);
         } else {
@@ -661,7 +661,7 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
         }
     }
     cluster.sync();   // the other CTAs read this one's ysl until here
-    if (a.red) ep_reduce_epilogue(a.red, s_epoch, y, a.y_f16, a.hidden);
+    if (a.red) ep_reduce_epilogue(a.red, s_epoch, peers, y, a.y_f16, a.hidden);
 }
 
 // --------------------------- register-direct passes (hidden/inter > 4096) ----
@@ -999,7 +999,9 @@ int down_mma(const MoEMaps& mp, const MoEArgs& a, const uint32_t* idx, const flo
     at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    // with the fused reduction the pass reads the call number the previous
+    // fused call wrote last: strict stream order, as every fused kernel
+    cfg.numAttrs = pdl_enabled() && !a.red ? 2 : 1;
     const int sp = span_bytes((uint32_t)a.inter / 32);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_down_mma<LAYOUT, NW>, mp, a, idx, wgt, local,
                                              (const uint4*)h, xsh, y, tiles_max, sp);

@@ -107,6 +107,15 @@ __device__ __forceinline__ int tile_row_of(int g) {
     return WPG == 4 ? (g >> 1) + 4 * (g & 1) : (g < 4 ? 2 * g : 2 * (g - 4) + 1);
 }
 
+// An L2 policy under which the lines a copy brings in are evicted first: for
+// streams read once per call (weights, their scales), so that they do not push
+// out what is read again (activations, outputs, small tables).
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // Brings a tensor map's descriptor into the TMA unit's cache ahead of use.
 __device__ __forceinline__ void prefetch_tmap(const void* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -124,6 +133,23 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int x
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
         "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+// The same copies with an L2 cache policy (l2_evict_first()).
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const void* map, int x, int y,
+                                                 uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst), "l"(map), "r"(x), "r"(y),
+        "r"(bar), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const void* map, int x, int y,
+                                                 int z, uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(dst), "l"(map), "r"(x),
+        "r"(y), "r"(z), "r"(bar), "l"(pol)
         : "memory");
 }
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int x, int y, int z,
@@ -171,6 +197,9 @@ __device__ __forceinline__ SpanCopy span_copy(uint32_t dst, const uint8_t* p, ui
 }
 __device__ __forceinline__ void bulk_copy(const SpanCopy& c, uint32_t bar) {
     if (c.bytes) bulk_g2s(c.dst, c.src, c.bytes, bar);
+}
+__device__ __forceinline__ void bulk_copy_hint(const SpanCopy& c, uint32_t bar, uint64_t pol) {
+    if (c.bytes) bulk_g2s_hint(c.dst, c.src, c.bytes, bar, pol);
 }
 
 // Where a unit's scales sit: entry G of tile row R, array a, at
@@ -370,10 +399,11 @@ struct XStage {
 
 template <int WPG>
 __device__ __forceinline__ void stage_x(const uint4* __restrict__ x, int n,
-                                        const float* __restrict__ xs_in, uint4* xf, float2* gc) {
+                                        const float* __restrict__ xs_in, uint4* xf, float2* gc,
+                                        const float* __restrict__ x32 = nullptr) {
     XStage<WPG> st;
-    st.load(x, n);
-    st.store(x, n, xs_in, xf, gc);
+    st.load(x, n, x32);
+    st.store(x, n, xs_in, xf, gc, x32);
 }
 
 // Wait for a slot phase, bounded in time (2 s); false (and an error bit) if

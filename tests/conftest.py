@@ -60,8 +60,29 @@ def norm_rel(got, ref) -> float:
     return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
 
 
+def elem_rel(got, ref, floor: float = 1e-2) -> float:
+    """Largest per-element relative error |got - ref| / |ref| over the outputs
+    with |ref| >= floor * max|ref| (BASELINE's "max relative error"); the few
+    outputs that sit near zero are held by norm_rel instead."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    keep = np.abs(ref) >= floor * max(np.max(np.abs(ref)), 1e-30)
+    if not keep.any():
+        return 0.0
+    return float(np.max(np.abs(got[keep] - ref[keep]) / np.abs(ref[keep])))
+
+
 # BASELINE: max relative error <= 1e-3 for outputs with fp32 accumulation.  The
 # error is taken relative to the largest reference output, as the reference's
 # own check does; per-element relative error is meaningless for outputs that
 # sit near zero.
 TOL = 1e-3
+# Per element (elem_rel, over the outputs with |ref| >= 1e-2 max|ref|) the GEMV
+# outputs are held to the reference's own tolerance, 2e-3
+# (int4-gemv/src/main.mm:476), taken per element instead of over the max-norm.
+# Two effects sit between 1e-3 and 2e-3 for the smallest of those outputs:
+# rounding an fp64 value to fp16 moves it by up to 2^-11 (4.9e-4) of itself,
+# and the int4 decode feeds the tensor cores 1024+q (the exponent trick), so
+# the fp32 partial sums are ~1024x the signal and carry an absolute error of
+# about 1e-5 of the largest output (measured 0.6-1.1e-3 per element).
+TOL_ELEM = 2e-3

@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import TOL, norm_rel
+from conftest import TOL, TOL_ELEM, elem_rel, norm_rel
 
 pytestmark = pytest.mark.gpu
 
@@ -35,6 +35,7 @@ def test_batched_vs_oracle(lib, M, K, G, B):
     for b in range(B):
         ref = oracle.gemv_int4_sb(Wn, SBn, host(X[b]).view(np.uint16), G)
         assert norm_rel(got[b], ref) <= TOL, b
+        assert elem_rel(got[b], ref) <= TOL_ELEM, b
 
 
 def test_batched_matches_the_gemv(lib):

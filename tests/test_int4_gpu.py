@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import TOL, golden, norm_rel
+from conftest import TOL, TOL_ELEM, elem_rel, golden, norm_rel
 
 pytestmark = pytest.mark.gpu
 
@@ -80,9 +80,37 @@ def test_baseline_shapes_f16out_and_f32(lib, M, K):
     ref = oracle.gemv_int4_sb(host(w["W"]).view(np.uint32), host(w["SB"]).view(np.uint16),
                               host(x).view(np.uint16), 64)
     assert norm_rel(host(y16).astype(np.float32), ref) <= TOL
+    assert elem_rel(host(y16).astype(np.float32), ref) <= TOL_ELEM
     assert norm_rel(got32, ref) <= TOL
     # fp32 accumulation: the fp32 output is far inside the tolerance
     assert norm_rel(got32, ref) <= 5e-5
+    assert elem_rel(got32, ref) <= TOL_ELEM
+
+
+@pytest.mark.parametrize("B", [1, 8])
+def test_config4_lmhead_full_shape(lib, B):
+    """BASELINE config 4's lm_head, 201088 x 2880, at full size on one GPU: the
+    batch-1 GEMV (scale rows of 180 B, not 16-byte strided, so it runs through
+    the batched kernel's per-tile scale copies) and the batch-8 probe."""
+    import torch
+    import kernels_b200 as kb
+    from kernels_b200 import synth
+    M, K = 201088, 2880
+    w, _ = baseline_case(kb, M, K, seed=4)
+    P = kb.gemv_params(M, K, 64)
+    X = torch.stack([synth.activations(K, seed=70 + b) for b in range(B)])
+    Y = torch.full((B, M), float("nan"), dtype=torch.float16, device="cuda")
+    if B == 1:
+        kb.gemv_int4_sb_f16out(w["W"], w["SB"], X[0], Y[0], P)
+    else:
+        kb.gemm_int4_sb_f16(w["W"], w["SB"], X, Y, B, P)
+    got = host(Y).astype(np.float32)
+    Wn, SBn = host(w["W"]).view(np.uint32), host(w["SB"]).view(np.uint16)
+    for b in range(B):
+        ref = oracle.gemv_int4_sb(Wn, SBn, host(X[b]).view(np.uint16), 64)
+        assert np.isfinite(got[b]).all(), b
+        assert norm_rel(got[b], ref) <= TOL, b
+        assert elem_rel(got[b], ref) <= TOL_ELEM, b
 
 
 @pytest.mark.parametrize("M,K,G", [(1, 32, 32), (7, 64, 32), (33, 96, 96), (130, 2880, 64),
@@ -102,6 +130,7 @@ def test_edge_shapes(lib, M, K, G):
     got, _ = run_v6(kb, dev(W), dev(SB.view(np.uint16)), dev(x.view(np.uint16)), P)
     ref = oracle.gemv_int4_sb(W, SB.view(np.uint16), x.view(np.uint16), G)
     assert norm_rel(got, ref) <= TOL
+    assert elem_rel(got, ref) <= TOL_ELEM
 
 
 def test_deterministic_and_stream_ordered(lib):

@@ -107,6 +107,9 @@ def test_baseline_config3_full_size(lib, seed):
     assert_separated(logits, P.top_k)
     assert np.array_equal(host(ws.tensor("idx", torch.int32, 4)).view(np.uint32), idx)
     assert np.allclose(host(ws.tensor("wgt", torch.float32, 4)), wgt, rtol=1e-5, atol=1e-6)
+    # max-norm, as the reference checks its block (moe-fused/src/main.mm:336-376): the
+    # kernels keep h in fp16 as the reference's do, the fp64 oracle does not round it, so
+    # outputs near zero carry that rounding and a per-element bound means nothing there
     assert norm_rel(host(y).astype(np.float32), yref) <= TOL
 
 

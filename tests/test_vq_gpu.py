@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import TOL, golden, norm_rel
+from conftest import TOL, TOL_ELEM, elem_rel, golden, norm_rel
 
 pytestmark = pytest.mark.gpu
 
@@ -59,6 +59,7 @@ def test_baseline_rowscale(lib, M, K, y_f16):
                          host(x).view(np.uint16))
     got = host(y).astype(np.float32)
     assert norm_rel(got, ref) <= TOL
+    assert elem_rel(got, ref) <= TOL_ELEM
     if not y_f16:
         assert norm_rel(got, ref) <= 5e-5
 
