@@ -241,12 +241,44 @@ struct XWin {
     __host__ __device__ static int uint4s(int K) { return (K / (256 * WPG) + 1) * STRIDE; }
 };
 
+// Shared-memory loads by 32-bit shared address (the tile engine keeps its
+// addresses in 32 bits: one integer add per load, no 64-bit pointer math).
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(a));
+    return v;
+}
+template <int WPG>
+__device__ __forceinline__ void lds_words(uint32_t a, uint32_t (&w)[WPG]) {
+    if (WPG == 1) {
+        w[0] = lds32(a);
+    } else if (WPG == 2) {
+        const uint2 v = lds64(a);
+        w[0] = v.x; w[WPG - 1] = v.y;
+    } else {
+        const uint4 v = lds128(a);
+        w[0] = v.x; w[1 % WPG] = v.y; w[2 % WPG] = v.z; w[3 % WPG] = v.w;
+    }
+}
+
 // Per-lane constants of the tile engine (fixed for a warp's lifetime).
 template <int WPG>
 struct LaneGeom {
     int R;         // tile row read for MMA row g (and R+8 for row g+8)
     int offs[8];   // byte offset of this lane's words of group j, tile row R
-    int xoff[8];   // uint4 offset of this lane's x fragments for step j
+    int xoff[8];   // byte offset of this lane's x fragments for step j
     __device__ __forceinline__ void init(int lane) {
         const int g = lane >> 2, t = lane & 3;
         R = tile_row_of<WPG>(g);
@@ -255,7 +287,7 @@ struct LaneGeom {
         for (int j = 0; j < kWindow; ++j) {
             const int o = 16 * WPG * j + lo;   // byte in the row's 128*WPG
             offs[j] = (o >> 7) * (kTileRows * 128) + R * 128 + ((((o >> 4) & 7) ^ X) << 4) + (o & 15);
-            xoff[j] = g == j ? (4 * j + t) * WPG : XWin<WPG>::WORDS;
+            xoff[j] = 16 * (g == j ? (4 * j + t) * WPG : XWin<WPG>::WORDS);
         }
     }
 };
@@ -267,45 +299,51 @@ __device__ __forceinline__ void tile_dot_w(const uint8_t* slot, const uint8_t* s
                                            uint32_t scap, float (&acc)[2]) {
     using SG = ScaleGeom<LAYOUT>;
     const int t = lane & 3;
-    // one accumulator pair per word position: 2*WPG independent MMA chains
-    float de[WPG][4], dd[WPG][4];
-#pragma unroll
-    for (int i = 0; i < WPG; ++i)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) de[i][q] = dd[i][q] = 0.f;
+    const uint32_t sa = smem_u32(slot), xa = smem_u32(xwin);
+    // two MMA chains: the even nibbles (1024+q) and the odd ones (1024+16q)
+    float de[4] = {0.f, 0.f, 0.f, 0.f}, dd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < kWindow; ++j) {
         if (FULL || j < ng) {
-            const uint4* xp = xwin + lg.xoff[j];
+            const uint32_t pa = sa + (uint32_t)lg.offs[j], px = xa + (uint32_t)lg.xoff[j];
             uint32_t wa[WPG], wb[WPG];
-            load_words<WPG>(slot + lg.offs[j], wa);
-            load_words<WPG>(slot + lg.offs[j] + 8 * 128, wb);
+            lds_words<WPG>(pa, wa);
+            lds_words<WPG>(pa + 8 * 128, wb);
 #pragma unroll
             for (int i = 0; i < WPG; ++i) {
-                const uint4 xv = xp[i];
+                const uint4 xv = lds128(px + 16 * i);
                 uint32_t ae0, ae1, ao0, ao1, be0, be1, bo0, bo1;
                 decode_word(wa[i], ae0, ae1, ao0, ao1);
                 decode_word(wb[i], be0, be1, bo0, bo1);
-                mma_16816(de[i], ae0, be0, ae1, be1, xv.x, xv.y);
-                mma_16816(dd[i], ao0, bo0, ao1, bo1, xv.z, xv.w);
+                mma_16816(de, ae0, be0, ae1, be1, xv.x, xv.y);
+                mma_16816(dd, ao0, bo0, ao1, bo1, xv.z, xv.w);
             }
         }
     }
     // column 2t+c of the accumulators is group 2t+c; [q]: tile row R + 8*(q>>1)
-    const uint8_t* s0 = sc + sv.so[0] + lg.R * sv.rs[0] + SG::ES * 2 * t;
-    const uint8_t* b0 = sc + scap + sv.so[1] + lg.R * sv.rs[1] + SG::ES * 2 * t;
-    const float4 kk = *reinterpret_cast<const float4*>(gc + 2 * t);   // groups 2t, 2t+1
+    const uint32_t s0 = smem_u32(sc) + sv.so[0] + lg.R * sv.rs[0] + SG::ES * 2 * t;
+    const uint32_t b0 = smem_u32(sc) + scap + sv.so[1] + lg.R * sv.rs[1] + SG::ES * 2 * t;
+    const uint4 kq = lds128(smem_u32(gc + 2 * t));   // (off, sum x) of groups 2t, 2t+1
+    const float4 kk = make_float4(__uint_as_float(kq.x), __uint_as_float(kq.y),
+                                  __uint_as_float(kq.z), __uint_as_float(kq.w));
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        float e = de[0][q], o = dd[0][q];
-#pragma unroll
-        for (int i = 1; i < WPG; ++i) { e += de[i][q]; o += dd[i][q]; }
         const int c = q & 1, r = q >> 1;
         if (FULL || 2 * t + c < ng) {
             const float off = c ? kk.z : kk.x, xsum = c ? kk.w : kk.y;
-            const float d = fmaf(o, 0.0625f, e) - off;
-            const float2 sb = scale_pair<LAYOUT>(s0 + r * 8 * sv.rs[0] + SG::ES * c,
-                                                 b0 + r * 8 * sv.rs[1] + SG::ES * c);
+            const float d = fmaf(dd[q], 0.0625f, de[q]) - off;
+            const uint32_t sp = s0 + r * 8 * sv.rs[0] + SG::ES * c;
+            float2 sb;
+            if (LAYOUT == kSBHalf2) {
+                const uint32_t v = lds32(sp);
+                sb = __half22float2(*reinterpret_cast<const __half2*>(&v));
+            } else {
+                const uint32_t bp = b0 + r * 8 * sv.rs[1] + SG::ES * c;
+                const uint32_t sv16 = lds32(sp & ~3u) >> (8 * (sp & 2));
+                const uint32_t bv16 = lds32(bp & ~3u) >> (8 * (bp & 2));
+                sb = LAYOUT == kSepF16 ? make_float2(h2f((uint16_t)sv16), h2f((uint16_t)bv16))
+                                       : make_float2(bf2f((uint16_t)sv16), bf2f((uint16_t)bv16));
+            }
             acc[r] = fmaf(sb.x, d, fmaf(sb.y, xsum, acc[r]));
         }
     }
@@ -337,13 +375,17 @@ __device__ __forceinline__ float quad_sum(float v) {
 // Stages x (n fp16 values, 16-byte aligned) as word fragments in the XWin
 // layout (zero fragments included), and the per-group constants (off, sum x)
 // for groups of WPG*32; xs_in, if given, supplies the per-32 sums of x for
-// the bias term.  One thread per group.  Split in two so that the loads can
-// be issued ahead of a TMA burst (which would otherwise queue in front of
-// them) and finished after it:  XStage<WPG> st; st.load(...); ...; st.store(...).
-// All threads of the CTA call both; no barrier inside (the caller syncs).
+// the bias term.  One thread per 16-byte word of x (a round of blockDim words
+// at a time); a group's 4*WPG words sit on consecutive lanes, whose sums meet
+// by shuffles.  Split in two so that the loads can be issued ahead of a TMA
+// burst (which would otherwise queue in front of them) and finished after it:
+// XStage<WPG> st; st.load(...); ...; st.store(...).  All threads of the CTA
+// call both; no barrier inside (the caller syncs).
 template <int WPG>
 struct XStage {
-    uint4 v[4 * WPG];
+    static constexpr int kHold = 4;   // rounds of words a thread loads ahead
+    static constexpr int GW = 4 * WPG;   // words per group
+    uint4 v[kHold];
     // 8 fp16 values of x as one 16-byte word: x16 as given, or x32 rounded
     __device__ __forceinline__ static uint4 word(const uint4* __restrict__ x16,
                                                  const float* __restrict__ x32, int i) {
@@ -357,39 +399,54 @@ struct XStage {
     // x16: fp16 activations, or x32 (if non-null): fp32 activations, rounded to fp16
     __device__ __forceinline__ void load(const uint4* __restrict__ x, int n,
                                          const float* __restrict__ x32 = nullptr) {
-        const int G = threadIdx.x;
-        if (G < n / (32 * WPG)) {
+        const int words = n / 8;
 #pragma unroll
-            for (int i = 0; i < 4 * WPG; ++i) v[i] = word(x, x32, 4 * WPG * G + i);
+        for (int r = 0; r < kHold; ++r) {
+            const int wd = r * (int)blockDim.x + (int)threadIdx.x;
+            if (wd < words) v[r] = word(x, x32, wd);
         }
     }
-    __device__ __forceinline__ void store(const uint4* __restrict__ x, int n,
-                                          const float* __restrict__ xs_in, uint4* xf,
-                                          float2* gc, const float* __restrict__ x32 = nullptr) {
+    // One round: word wd (if on) into its window slot; the group's sums.
+    __device__ __forceinline__ static void one(uint4 raw, int wd, bool on,
+                                               const float* __restrict__ xs_in, uint4* xf,
+                                               float2* gc) {
         using XW = XWin<WPG>;
-        const int ng = n / (32 * WPG);
-        for (int G = threadIdx.x; G < ng; G += blockDim.x) {
-            if (G != (int)threadIdx.x) {   // more groups than threads: load here
+        float e = 0.f, o = 0.f;
+        if (on) {
+            const int w = wd / XW::WORDS;
+            const uint4 f = frag_of(raw);
+            xf[w * XW::STRIDE + (wd - w * XW::WORDS)] = f;
+            frag_sums(f, e, o);
+        }
 #pragma unroll
-                for (int i = 0; i < 4 * WPG; ++i) v[i] = word(x, x32, 4 * WPG * G + i);
-            }
-            float e = 0.f, o = 0.f;
-#pragma unroll
-            for (int i = 0; i < 4 * WPG; ++i) {
-                const int wd = 4 * WPG * G + i, w = wd / XW::WORDS;
-                const uint4 f = frag_of(v[i]);
-                xf[w * XW::STRIDE + (wd - w * XW::WORDS)] = f;
-                float ei, oi;
-                frag_sums(f, ei, oi);
-                e += ei;
-                o += oi;
-            }
+        for (int m = 1; m < GW; m <<= 1) {
+            e += __shfl_xor_sync(0xffffffffu, e, m);
+            o += __shfl_xor_sync(0xffffffffu, o, m);
+        }
+        if (on && (wd & (GW - 1)) == 0) {
+            const int G = wd / GW;
             float s = e + o;
             if (xs_in) {
                 s = 0.f;
                 for (int c = 0; c < WPG; ++c) s += xs_in[WPG * G + c];
             }
             gc[G] = make_float2(fmaf(1024.f, e, 64.f * o), s);
+        }
+    }
+    __device__ __forceinline__ void store(const uint4* __restrict__ x, int n,
+                                          const float* __restrict__ xs_in, uint4* xf,
+                                          float2* gc, const float* __restrict__ x32 = nullptr) {
+        using XW = XWin<WPG>;
+        const int words = n / 8, nt = (int)blockDim.x;
+#pragma unroll
+        for (int r = 0; r < kHold; ++r) {
+            const int wd = r * nt + (int)threadIdx.x;
+            if (r * nt < words) one(v[r], wd, wd < words, xs_in, xf, gc);
+        }
+        for (int r = kHold; r * nt < words; ++r) {   // long rows: loaded here
+            const int wd = r * nt + (int)threadIdx.x;
+            one(wd < words ? word(x, x32, wd) : make_uint4(0, 0, 0, 0), wd, wd < words, xs_in,
+                xf, gc);
         }
         const int nwin = n / (256 * WPG) + 1;
         for (int i = threadIdx.x; i < nwin * WPG; i += blockDim.x)
