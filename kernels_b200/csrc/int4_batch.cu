@@ -230,14 +230,17 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemm_batch_kernel(
         }
         mbar_arrive_expect_tx(bar, bytes);
         fence_proxy_async_smem();
+        // weights stream once per call: evicted first from L2
+        const uint64_t pol = l2_evict_first();
         if (a.map3) {
-            tma_load_3d(cd, &a.wmap, 0, row0, c0 / 8, bar);
+            tma_load_3d_hint(cd, &a.wmap, 0, row0, c0 / 8, bar, pol);
         } else {
             for (int sg = 0; sg < nseg; ++sg)
-                tma_load_2d(cd + sg * kTileRows * 128, &a.wmap, 4 * c0 + 32 * sg, row0, bar);
+                tma_load_2d_hint(cd + sg * kTileRows * 128, &a.wmap, 4 * c0 + 32 * sg, row0, bar,
+                                 pol);
         }
-        if (a.scale_map) tma_load_2d(sd, &a.smap, g0, row0, bar);
-        else if (sc0.bytes) bulk_copy(sc0, bar);
+        if (a.scale_map) tma_load_2d_hint(sd, &a.smap, g0, row0, bar, pol);
+        else if (sc0.bytes) bulk_copy_hint(sc0, bar, pol);
     };
     // The weights are constants: each warp's first unit streams before the
     // previous kernel on the stream has finished; the rest of the ring waits

@@ -394,12 +394,14 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_gate_up_mma(
         if (lane != 0) return;
         mbar_arrive_expect_tx(bar, (uint32_t)nseg * kTileRows * 128);
         fence_proxy_async_smem();
+        // expert weights stream once per token: evicted first from L2
+        const uint64_t pol = l2_evict_first();
         if (c0 / 8 + WPG <= mp.gu_segs) {
-            tma_load_5d(cd, &mp.gu5, 0, itm.y * kTileRows, c0 / 8, proj, itm.z, bar);
+            tma_load_5d_hint(cd, &mp.gu5, 0, itm.y * kTileRows, c0 / 8, proj, itm.z, bar, pol);
         } else {
             for (int sg = 0; sg < nseg; ++sg)
-                tma_load_4d(cd + sg * kTileRows * 128, &mp.gu, 4 * c0 + 32 * sg,
-                            itm.y * kTileRows, proj, itm.z, bar);
+                tma_load_4d_hint(cd + sg * kTileRows * 128, &mp.gu, 4 * c0 + 32 * sg,
+                                 itm.y * kTileRows, proj, itm.z, bar, pol);
         }
     };
     for (int i = 0; i < kDepth && i < mine; ++i) {
@@ -574,12 +576,15 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
         if (lane != 0) return;
         mbar_arrive_expect_tx(bar, (uint32_t)nseg * kTileRows * 128);
         fence_proxy_async_smem();
+        // expert weights stream once per token: evicted first from L2
+        const uint64_t pol = l2_evict_first();
         if (c0 / 8 + WPG <= mp.dn_segs) {
-            tma_load_4d(cd, &mp.dn4, 0, (T0 + u.k) * kTileRows, c0 / 8, tab->le[p], bar);
+            tma_load_4d_hint(cd, &mp.dn4, 0, (T0 + u.k) * kTileRows, c0 / 8, tab->le[p], bar,
+                             pol);
         } else {
             for (int sg = 0; sg < nseg; ++sg)
-                tma_load_3d(cd + sg * kTileRows * 128, &mp.dn, 4 * c0 + 32 * sg,
-                            (T0 + u.k) * kTileRows, tab->le[p], bar);
+                tma_load_3d_hint(cd + sg * kTileRows * 128, &mp.dn, 4 * c0 + 32 * sg,
+                                 (T0 + u.k) * kTileRows, tab->le[p], bar, pol);
         }
     };
     // the down rows first: they do not depend on the gate/up pass

@@ -152,6 +152,22 @@ __device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const void* map, 
         "r"(y), "r"(z), "r"(bar), "l"(pol)
         : "memory");
 }
+__device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const void* map, int x, int y,
+                                                 int z, int w, uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst), "l"(map), "r"(x),
+        "r"(y), "r"(z), "r"(w), "r"(bar), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_5d_hint(uint32_t dst, const void* map, int x, int y,
+                                                 int z, int w, int v, uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(dst), "l"(map),
+        "r"(x), "r"(y), "r"(z), "r"(w), "r"(v), "r"(bar), "l"(pol)
+        : "memory");
+}
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int x, int y, int z,
                                             int w, uint32_t bar) {
     asm volatile(

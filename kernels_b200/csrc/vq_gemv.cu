@@ -242,14 +242,17 @@ __global__ void __launch_bounds__(NW * 32, 1) vq_tile_kernel(const __grid_consta
     auto slot = [&](int k) { return smem_u32(ring + (warp * D + k) * kSlotIdx); };
     auto sslot = [&](int k) { return smem_u32(sring + (warp * D + k) * kSlotScale); };
     auto bar = [&](int k) { return smem_u32(&full[warp * kVqMaxDepth + k]); };
+    // indices and scales are read once per call: evicted first from L2, so that
+    // x, the codebook and the outputs stay cached
+    const uint64_t pol = l2_evict_first();
     auto issue = [&](const It& u, int k) {
         const uint32_t dst = slot(k), sdst = SMAP ? sslot(k) : 0u, b = bar(k);
         const int row0 = r0 + kTileRows * u.tile;
         if (lane != 0) return;
         mbar_arrive_expect_tx(b, kSlotIdx + (SMAP ? kSlotScale : 0));
         fence_proxy_async_smem();
-        tma_load_2d(dst, &a.imap, 32 * u.part, row0, b);
-        if (SMAP) tma_load_2d(sdst, &a.smap, 8 * u.part, row0, b);
+        tma_load_2d_hint(dst, &a.imap, 32 * u.part, row0, b, pol);
+        if (SMAP) tma_load_2d_hint(sdst, &a.smap, 8 * u.part, row0, b, pol);
     };
     // the indices (and scales) are constants of the model: the ring fills
     // before the previous kernel on the stream has finished
