@@ -723,15 +723,28 @@ def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status,
     wsp = kb.MoEWorkspace(Pm)
     fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=True,
                         n_experts=128)
-    t = Timer(torch, lambda i: kb.moe_block_ep(comm, shard, R, xs_[i % 16], y, Pm, fmt, wsp), 200)
-    t.build(200)
-    barrier()
-    t.run(200)
-    steps = 2000
-    dt = slowest(t.time(steps, barrier))
-    d["moe_config3_ep"] = {"us_per_token": round(dt / steps * 1e6, 3),
+    ep = {}
+    # the NCCL form (ncclAllReduce of the fp32 partials) beside the default
+    for form in (["fused", "nccl"] if comm.fused else ["nccl"]):
+        comm.set_fused(form == "fused")
+        torch.cuda.synchronize()
+        barrier()
+        t = Timer(torch, lambda i: kb.moe_block_ep(comm, shard, R, xs_[i % 16], y, Pm, fmt, wsp),
+                  200)
+        t.build(200)
+        barrier()
+        t.run(200)
+        steps = 2000
+        ep[form] = round(slowest(t.time(steps, barrier)) / steps * 1e6, 3)
+        del t
+        torch.cuda.synchronize()
+        barrier()
+    comm.set_fused(True)
+    d["moe_config3_ep"] = {"us_per_token": ep.get("fused", ep["nccl"]),
+                           "nccl_us_per_token": ep["nccl"],
+                           "reduce": ("fused into the down pass over peer memory" if "fused" in ep
+                                      else "ncclAllReduce"),
                            "experts_per_gpu": e_hi - e_lo, "allreduce": "fp32 y[2880]"}
-    del t
     status("detail_moe_ep")
     # parity: one token; every rank's y must be bit-identical, and rank 0 checks
     # it and the selected experts against the oracle over the whole pool

@@ -350,6 +350,11 @@ class Comm:
         peer has given up; sticky until the communicator is re-created."""
         call("graft_comm_status", self.handle)
 
+    def set_fused(self, on: bool) -> None:
+        """Fused (peer-memory) forms on, or off so that every call runs its NCCL
+        form; every rank must make the same setting."""
+        call("graft_comm_set_fused", self.handle, int(bool(on)))
+
     def set_wait_limit(self, ns: int) -> None:
         """Time limit of every peer wait of the fused calls (ns; 4 s by default)."""
         call("graft_comm_set_wait_limit", self.handle, ns)

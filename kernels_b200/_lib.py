@@ -124,6 +124,7 @@ SIGNATURES: dict[str, tuple] = {
     "graft_comm_alloc": (INT, [P, SIZE, C.POINTER(P)]),
     "graft_comm_free": (INT, [P, P]),
     "graft_comm_fused": (INT, [P]),
+    "graft_comm_set_fused": (INT, [P, INT]),
     "graft_comm_status": (INT, [P]),
     "graft_comm_set_wait_limit": (INT, [P, U64]),
     "graft_gemv_int4_sharded": (INT, [P, P, P, P, P, C.POINTER(GemvParams), P]),

@@ -472,44 +472,6 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_gate_up_mma(
 // order and the output bias; then the CTAs combine the experts' rows in slot
 // order through distributed shared memory, weighted by the router weights
 // (fused_down_combine, moe-fused/src/kernels.metal:253-262).
-// Expert-parallel all-reduce in the down pass's epilogue.  Every CTA has
-// stored its rows of this rank's partial output into slot `rank` of every
-// rank's copy of the symmetric reduce buffer; here it publishes them to each
-// peer (one release add per peer), and the grid's last CTA waits (bounded)
-// until every peer's CTAs have published, sums the slots in rank order -- the
-// same order on every rank, so every rank gets the same bits -- into y and
-// closes call E.  The handshake is the fused gather's (graft_p2p.cuh).
-__device__ void ep_reduce_epilogue(const graft::P2PGather* g, uint32_t E, bool wrote_peers,
-                                   void* y, int y_f16, int n) {
-    using namespace graft::dev;
-    __shared__ int s_last;
-    __syncthreads();
-    if (wrote_peers && (int)threadIdx.x < g->nranks && (int)threadIdx.x != g->rank)
-        red_release_sys(g->peer_cnt[threadIdx.x] + g->rank, 1u);
-    if (threadIdx.x == 0) {
-        __threadfence();
-        s_last = atomicAdd(g->done_count, 1u) == gridDim.x - 1;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    // the last CTA here: every peer's CTAs have published their slots
-    if (threadIdx.x < 32) warp_wait_counts(g, gridDim.x, 2u);
-    __syncthreads();
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    const float* slots = reinterpret_cast<const float*>(g->buf[g->rank]);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float v = 0.f;
-        for (int r = 0; r < g->nranks; ++r) v += __ldcg(slots + (size_t)r * graft::kReduceMaxFloats + i);
-        if (y_f16) reinterpret_cast<__half*>(y)[i] = __float2half_rn(v);
-        else reinterpret_cast<float*>(y)[i] = v;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        *g->done_count = 0;
-        *reinterpret_cast<volatile uint32_t*>(g->epoch) = E;
-    }
-}
-
 template <int LAYOUT, int NW>
 __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
     const __grid_constant__ MoEMaps mp, const MoEArgs a, const uint32_t* __restrict__ idx,
@@ -594,10 +556,7 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
     }
     pdl_wait();   // h comes from the gate/up pass
     __shared__ uint32_t s_epoch;   // the expert-parallel reduction's call number
-    if (a.red) {
-        const uint32_t E = graft::dev::gather_enter(a.red);
-        if (threadIdx.x == 0) s_epoch = E;
-    }
+    if (a.red && threadIdx.x == 0) s_epoch = graft::dev::fused_call(a.red);
     if (act) {
         const int j = tab->j[p];
         stage_x<WPG>(h + (size_t)j * (a.inter / 8), a.inter,
@@ -648,25 +607,43 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
         }
     cluster.sync();
     const int ns = tab->n;
-    // the peers must have entered this call before their buffers are written
-    // (false: one never did -- only this rank's slot copy is written)
-    const bool peers = a.red ? graft::dev::gather_wait_entry(a.red, s_epoch) : false;
+    const graft::P2PGather* g = a.red;
+    const uint32_t E = g ? s_epoch : 0u;
+    const bool ex = g && g->nranks > 1 && !graft::dev::poisoned(g);
+    const uint64_t t0 = ex ? graft::dev::global_ns() : 0ull;
     for (int q = p * NW * 32 + threadIdx.x; q < nt * kTileRows; q += ncl_cta * NW * 32) {
         float acc = 0.f;
         for (int e = 0; e < ns; ++e) acc += wgt[tab->j[e]] * cluster.map_shared_rank(ysl, e)[q];
         const int m = T0 * kTileRows + q;
-        if (a.red) {
-            for (int r = 0; r < a.red->nranks; ++r)
-                if (peers || r == a.red->rank)
-                    reinterpret_cast<float*>(a.red->buf[r])[(size_t)a.red->rank * graft::kReduceMaxFloats + m] = acc;
-        } else if (a.y_f16) {
-            reinterpret_cast<__half*>(y)[m] = __float2half_rn(acc);
-        } else {
-            reinterpret_cast<float*>(y)[m] = acc;
+        if (g) {
+            // Expert-parallel all-reduce: CTA c of every rank covers the same
+            // rows of y.  This rank's partial of row m goes to every peer as an
+            // LL pair in slot `rank`; the peers' partials of the row are polled
+            // from this rank's area and summed in rank order -- the same order
+            // on every rank, so every rank gets the same bits.
+            if (ex)
+                for (int r = 0; r < g->nranks; ++r)
+                    if (r != g->rank)
+                        graft::dev::ll_store1(graft::dev::ll_area(g, r, E) +
+                                                  8 * ((size_t)g->rank * graft::kReduceMaxFloats + m),
+                                              __float_as_uint(acc), E);
+            float v = 0.f;
+            for (int r = 0; r < g->nranks; ++r) {
+                uint32_t u = 0u;
+                if (r == g->rank) u = __float_as_uint(acc);
+                else if (ex)
+                    graft::dev::ll_load1(g, graft::dev::ll_area(g, g->rank, E) +
+                                              8 * ((size_t)r * graft::kReduceMaxFloats + m),
+                                         E, t0, u);
+                v += __uint_as_float(u);
+            }
+            acc = v;
         }
+        if (a.y_f16) reinterpret_cast<__half*>(y)[m] = __float2half_rn(acc);
+        else reinterpret_cast<float*>(y)[m] = acc;
     }
+    if (g) graft::dev::fused_close(g, E);
     cluster.sync();   // the other CTAs read this one's ysl until here
-    if (a.red) ep_reduce_epilogue(a.red, s_epoch, peers, y, a.y_f16, a.hidden);
 }
 
 // --------------------------- register-direct passes (hidden/inter > 4096) ----
@@ -1004,9 +981,9 @@ int down_mma(const MoEMaps& mp, const MoEArgs& a, const uint32_t* idx, const flo
     at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    // with the fused reduction the pass reads the call number the previous
-    // fused call wrote last: strict stream order, as every fused kernel
-    cfg.numAttrs = pdl_enabled() && !a.red ? 2 : 1;
+    // with the fused reduction too: the call number is read after the
+    // dependency wait (graft_p2p.cuh)
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     const int sp = span_bytes((uint32_t)a.inter / 32);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, moe_down_mma<LAYOUT, NW>, mp, a, idx, wgt, local,
                                              (const uint4*)h, xsh, y, tiles_max, sp);
