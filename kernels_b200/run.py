@@ -8,6 +8,7 @@ the counterpart of the reference harness binaries' flags (int4gemv --M --K --G
     python -m kernels_b200.run stream --mbytes 1024
     python -m kernels_b200.run batch --M 128256 --K 4096 --B 8
     python -m kernels_b200.run vqquant --M 4096 --K 4096
+    python -m kernels_b200.run expert [--copies 4]     # one gpt-oss expert (bf16 format)
 
 Each iteration is one launch on a rotating weight copy, timed with CUDA events;
 use it for small profiler captures (a few launches, a few GB).
@@ -20,7 +21,8 @@ import json
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["int4", "vq", "moe", "stream", "batch", "vqquant"])
+    ap.add_argument("kernel", choices=["int4", "vq", "moe", "stream", "batch", "vqquant",
+                                       "expert"])
     ap.add_argument("--M", type=int, default=4096)
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--G", type=int, default=64)
@@ -76,6 +78,16 @@ def main() -> None:
         W = torch.randn((a.M, a.K), generator=g, device="cuda", dtype=torch.float32) * 0.02
         nbytes = a.M * a.K * 4
         f = lambda i: kb.vq_quantize(W)  # noqa
+    elif a.kernel == "expert":
+        # moe-pipeline's per-expert forward: xsum32 (fp32 x), gemv_int4_bf16 (gate, up),
+        # SwiGLU, xsum32, gemv_int4_bf16 (down); rotating resident experts
+        P = kb.moe_params(2880, 2880, a.copies, 4)
+        pool, _ = synth.moe_pool(P, scale_f16=False, has_bias_out=True, act_f16=False, seed=11)
+        scratch = kb.ExpertScratchBuffers(P)
+        x = synth.activations(2880, seed=3).float()
+        y = torch.empty(2880, dtype=torch.float32, device="cuda")
+        nbytes = P.blob
+        f = lambda i: kb.expert_forward(pool[(i % a.copies) * P.blob:], x, y, P, scratch)  # noqa
     elif a.kernel == "moe":
         P = kb.moe_params(2880, 2880, a.experts, a.top_k)
         pool, R = synth.moe_pool(P, scale_f16=True, has_bias_out=False, act_f16=True)

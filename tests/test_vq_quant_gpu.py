@@ -1,6 +1,7 @@
 """GPU parity of the VQ quantiser (graft_vq_quantize) against its CPU checker
-(oracle/vq_quant.py): bit-exact codes, codebook and scales; then the
-quantised matrix through the VQ GEMV."""
+(oracle/vq_quant.py) and against the reference's own quantiser's golden
+vectors (tests/golden/vq_quant_ref_*.npz): bit-exact codes, codebook and
+scales; then the quantised matrix through the VQ GEMV."""
 from __future__ import annotations
 
 import numpy as np
@@ -8,7 +9,7 @@ import pytest
 
 import oracle
 from oracle import vq_quant as vq
-from conftest import TOL, norm_rel
+from conftest import GOLDEN, TOL, norm_rel
 
 pytestmark = pytest.mark.gpu
 
@@ -36,6 +37,23 @@ def test_quantize_bit_exact(lib, M, K, sub, iters, seed):
     assert np.array_equal(host(S).view(np.uint16), rS16)
     assert np.array_equal(host(Cb).view(np.uint16), rC16)
     assert np.array_equal(host(IDX), ridx)
+
+
+@pytest.mark.parametrize("name,M,K,sub", [("s4096", 64, 512, 4096), ("s8192", 96, 1024, 8192)])
+def test_quantize_matches_reference_golden(lib, name, M, K, sub):
+    """The reference's pq_quantize.quantize_matrix (run under tests/golden/mlx_np.py
+    with the same draws) produced these; the CUDA quantiser must give the same."""
+    import torch
+    import kernels_b200 as kb
+    g = np.load(GOLDEN / f"vq_quant_ref_{name}.npz")
+    rng = np.random.default_rng(M + K)
+    W = (rng.standard_normal((M, K)) * 0.02).astype(np.float32)
+    W[1, 32:64] = 0.0
+    W[M - 1, :32] = 0.0
+    IDX, Cb, S = kb.vq_quantize(torch.from_numpy(W).cuda(), iters=25, sub=sub, seed=0)
+    assert np.array_equal(host(S).view(np.uint16), g["S"])
+    assert np.array_equal(host(Cb).view(np.uint16), g["C"])
+    assert np.array_equal(host(IDX), g["idx"])
 
 
 def test_quantised_matrix_through_the_vq_gemv(lib):
