@@ -283,7 +283,10 @@ int graft_moe_fused_down_combine_at(const void* pool, const uint32_t* idx, const
                                     const void* h, float* y, const GraftMoEParams* P,
                                     const float* xsh, graft_stream_t stream);
 
-/* Scratch the three kernels pass between them, carved from one caller buffer. */
+/* Scratch the block's kernels pass between them, carved from one caller
+ * buffer.  `sync` holds the one-launch block's tagged words (router partials,
+ * split row sums, h): they carry the launch they belong to, so the region needs
+ * no reset between calls, but the caller must not write it. */
 typedef struct {
     uint32_t* idx;   /* [top_k] selected experts                           */
     float* wgt;      /* [top_k] softmax weights                            */
@@ -293,13 +296,21 @@ typedef struct {
     void* h;         /* fp16 [top_k][inter]                                */
     float* xsh;      /* [top_k * inter/32]                                 */
     float* ypart;    /* fp32 [hidden]: a rank's partial y (expert parallel) */
+    void* sync;      /* tagged words of the one-launch block               */
 } GraftMoEScratch;
 
 /* Bytes of scratch graft_moe_scratch_carve needs for P. */
 size_t graft_moe_scratch_bytes(const GraftMoEParams* P);
-/* Carves `base` (device memory, 256-byte aligned, graft_moe_scratch_bytes long). */
+/* Carves `base` (device memory, 256-byte aligned, graft_moe_scratch_bytes long).
+ * Host arithmetic only: nothing is written to the buffer. */
 int graft_moe_scratch_carve(void* base, size_t bytes, const GraftMoEParams* P,
                             GraftMoEScratch* out);
+/* Zeroes the scratch's `sync` region on `stream` (before the first block call
+ * with a new buffer, and again if the buffer was used for anything else).  A
+ * block call that finds a region it has not seen zeroes it itself, except
+ * inside a stream capture, where it runs the three-kernel block instead. */
+int graft_moe_scratch_init(const GraftMoEParams* P, const GraftMoEScratch* scratch,
+                           graft_stream_t stream);
 
 /* The whole block in three launches (router_topk, gate_up_swiglu,
  * down_combine), as encodeFused does (moe-fused/src/main.mm:176-206), in the
@@ -315,6 +326,14 @@ int graft_moe_block(const void* pool, const float* R, const float* x, float* y,
 int graft_moe_block_ex(const void* pool, const void* R, const void* x, void* y,
                        const GraftMoEParams* P, const GraftMoEFormat* fmt,
                        const GraftMoEScratch* scratch, graft_stream_t stream);
+
+/* graft_moe_block and graft_moe_block_ex run the block as ONE launch where the
+ * shapes allow it (the tile engine's shapes; one CTA per SM whose CTAs hand
+ * the router logits, split row sums and h to one another through the
+ * scratch's `sync` region), else as the three launches above.  on = 0 forces
+ * the three launches (for comparisons); returns the previous setting.
+ * Process-wide, not thread-safe against concurrent block calls. */
+int graft_moe_set_one_launch(int on);
 
 /* graft_moe_block_ex without a caller-provided scratch buffer -- for callers
  * that cannot call cudaMalloc (hosts that own all device memory through their

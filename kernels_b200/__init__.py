@@ -279,6 +279,9 @@ class MoEWorkspace:
         base = (self.buffer.data_ptr() + 255) & ~255
         self.scratch = MoEScratch()
         call("graft_moe_scratch_carve", base, n, C.byref(P), C.byref(self.scratch))
+        # the one-launch block's tagged words start from zero (on the current stream)
+        call("graft_moe_scratch_init", C.byref(P), C.byref(self.scratch),
+             _s(torch.cuda.current_stream()))
         self.P = P
 
     def tensor(self, name: str, dtype, numel: int):
@@ -299,6 +302,12 @@ def moe_block_ex(pool, R, x, y, P: MoEParams, fmt: MoEFormat | None, ws: MoEWork
                  stream=None) -> None:
     call("graft_moe_block_ex", _p(pool), _p(R), _p(x), _p(y), C.byref(P),
          C.byref(fmt) if fmt is not None else None, C.byref(ws.scratch), _s(stream))
+
+
+def moe_set_one_launch(on: bool) -> bool:
+    """Whether graft_moe_block(_ex) may run the block as one launch (the
+    default) or must use the three-kernel form; returns the previous setting."""
+    return bool(load().graft_moe_set_one_launch(1 if on else 0))
 
 
 # ----------------------------------------------------------- multi-GPU --

@@ -54,7 +54,7 @@ class MoEFormat(C.Structure):
 class MoEScratch(C.Structure):
     _fields_ = [("idx", C.c_void_p), ("wgt", C.c_void_p), ("local", C.c_void_p),
                 ("xh", C.c_void_p), ("h", C.c_void_p), ("xsh", C.c_void_p),
-                ("ypart", C.c_void_p)]
+                ("ypart", C.c_void_p), ("sync", C.c_void_p)]
 
 
 class ExpertParams(C.Structure):
@@ -112,6 +112,8 @@ SIGNATURES: dict[str, tuple] = {
     "graft_moe_fused_down_combine_at": (INT, [P, P, P, P, P, C.POINTER(MoEParams), P, P]),
     "graft_moe_scratch_bytes": (SIZE, [C.POINTER(MoEParams)]),
     "graft_moe_scratch_carve": (INT, [P, SIZE, C.POINTER(MoEParams), C.POINTER(MoEScratch)]),
+    "graft_moe_set_one_launch": (INT, [INT]),
+    "graft_moe_scratch_init": (INT, [C.POINTER(MoEParams), C.POINTER(MoEScratch), P]),
     "graft_moe_block": (INT, [P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEScratch), P]),
     "graft_moe_block_ex": (INT, [P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEFormat),
                                  C.POINTER(MoEScratch), P]),
