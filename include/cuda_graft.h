@@ -126,6 +126,13 @@ int graft_gemv_int4_bf16(const void* W, const void* S, const void* B, const void
  * larger B runs in chunks.  G = 32, 64 or 128; W and X 16-byte aligned. */
 int graft_gemm_int4_sb_f16(const void* W, const void* SB, const void* X, void* Y, uint32_t B,
                            const GraftGemvParams* P, graft_stream_t stream);
+/* on = 1: B = 9..16 with G = 64, K a multiple of 256 (up to about 5k) and
+ * 16-byte aligned W/SB/X run on the tcgen05 tensor cores (weights decoded
+ * into tensor memory, x in shared memory, fp32 accumulators in tensor
+ * memory) instead of the mma.sync tile engine.  Off by default: measured
+ * slower at 16 tokens (128 against 95 us on a 128256 x 4096 lm_head).
+ * Returns the previous setting. */
+int graft_gemm_set_tcgen05(int on);
 
 /* stream_read, int4-gemv/src/kernels.metal:262-283: reads nquads 16-byte words
  * of src once, XOR-folds them and stores to sink[0] only if the fold is

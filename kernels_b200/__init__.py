@@ -304,6 +304,13 @@ def moe_block_ex(pool, R, x, y, P: MoEParams, fmt: MoEFormat | None, ws: MoEWork
          C.byref(fmt) if fmt is not None else None, C.byref(ws.scratch), _s(stream))
 
 
+def gemm_set_tcgen05(on: bool) -> bool:
+    """Whether graft_gemm_int4_sb_f16 runs 9..16 tokens on the tcgen05 kernel
+    or (the default) keeps every shape on the mma.sync tile engine; returns
+    the previous setting."""
+    return bool(load().graft_gemm_set_tcgen05(1 if on else 0))
+
+
 def moe_set_one_launch(on: bool) -> bool:
     """Whether graft_moe_block(_ex) may run the block as one launch (the
     default) or must use the three-kernel form; returns the previous setting."""
