@@ -724,9 +724,12 @@ def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status,
     fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=True,
                         n_experts=128)
     ep = {}
-    # the NCCL form (ncclAllReduce of the fp32 partials) beside the default
-    for form in (["fused", "nccl"] if comm.fused else ["nccl"]):
-        comm.set_fused(form == "fused")
+    # the NCCL form (ncclAllReduce of the fp32 partials) beside the default, and
+    # the one-launch block with the fused reduction
+    was_one = kb.moe_set_one_launch(0)
+    for form in (["fused", "one_launch", "nccl"] if comm.fused else ["nccl"]):
+        comm.set_fused(form != "nccl")
+        kb.moe_set_one_launch(2 if form == "one_launch" else 0)
         torch.cuda.synchronize()
         barrier()
         t = Timer(torch, lambda i: kb.moe_block_ep(comm, shard, R, xs_[i % 16], y, Pm, fmt, wsp),
@@ -740,7 +743,9 @@ def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status,
         torch.cuda.synchronize()
         barrier()
     comm.set_fused(True)
+    kb.moe_set_one_launch(was_one)
     d["moe_config3_ep"] = {"us_per_token": ep.get("fused", ep["nccl"]),
+                           "one_launch_us_per_token": ep.get("one_launch"),
                            "nccl_us_per_token": ep["nccl"],
                            "reduce": ("fused into the down pass over peer memory" if "fused" in ep
                                       else "ncclAllReduce"),

@@ -337,8 +337,10 @@ int graft_moe_block_ex(const void* pool, const void* R, const void* x, void* y,
 /* graft_moe_block and graft_moe_block_ex run the block as ONE launch where the
  * shapes allow it (the tile engine's shapes; one CTA per SM whose CTAs hand
  * the router logits, split row sums and h to one another through the
- * scratch's `sync` region), else as the three launches above.  on = 0 forces
- * the three launches (for comparisons); returns the previous setting.
+ * scratch's `sync` region), else as the three launches above.  Bits of on:
+ * 1 = the whole block on one GPU, 2 = a rank's share of an expert-parallel
+ * block (graft_moe_block_ex on an expert sub-range, graft_moe_block_ep); the
+ * default is 0 (three launches) unless set.  Returns the previous setting.
  * Process-wide, not thread-safe against concurrent block calls. */
 int graft_moe_set_one_launch(int on);
 

@@ -311,10 +311,11 @@ def gemm_set_tcgen05(on: bool) -> bool:
     return bool(load().graft_gemm_set_tcgen05(1 if on else 0))
 
 
-def moe_set_one_launch(on: bool) -> bool:
-    """Whether graft_moe_block(_ex) may run the block as one launch (the
-    default) or must use the three-kernel form; returns the previous setting."""
-    return bool(load().graft_moe_set_one_launch(1 if on else 0))
+def moe_set_one_launch(on) -> int:
+    """Where the MoE block runs as one launch instead of three: True/1 the
+    whole block on one GPU, 2 a rank's share of an expert-parallel block, 3
+    both, False/0 neither.  Returns the previous setting (the same bits)."""
+    return int(load().graft_moe_set_one_launch(int(on)))
 
 
 # ----------------------------------------------------------- multi-GPU --

@@ -116,8 +116,11 @@ def main() -> int:
         Rn = R.cpu().numpy().view(np.uint16)
         ws = kb.MoEWorkspace(P)
         # three tokens back to back (the reduce slots and counts are reused call after
-        # call), fp32 y, then one with fp16 y (the epilogue's conversion branch)
-        for it, y_f16 in enumerate((False, False, False, True)):
+        # call), fp32 y, then one with fp16 y (the epilogue's conversion branch); as
+        # three launches, then as one launch per rank (the one-launch block)
+        for it, (y_f16, one) in enumerate([(False, 0), (False, 0), (False, 0), (True, 0),
+                                           (False, 2), (False, 2), (True, 2)]):
+            kb.moe_set_one_launch(one)
             xm = synth.activations(2880, seed=14 + it)
             fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=y_f16,
                                 n_experts=P.n_experts)
@@ -130,12 +133,14 @@ def main() -> int:
             got_idx = ws.tensor("idx", torch.int32, P.top_k).cpu().numpy().view(np.uint32)
             gm = ym.float().cpu().numpy()
             r1, r2 = rels(gm, yref)
-            print(f"rank {rank}: ep moe token {it} ({'f16' if y_f16 else 'f32'} y) "
+            print(f"rank {rank}: ep moe token {it} ({'f16' if y_f16 else 'f32'} y, "
+                  f"{'one launch' if one else 'three launches'}) "
                   f"max|d|/max|ref| = {r1:.2e} elem {r2:.2e} top-k {list(got_idx)}", flush=True)
             # max-norm for the block, as the reference checks it (moe-fused/src/main.mm:336-376):
             # h is fp16 in the kernels, as in the reference's, and fp64 in the oracle
             ok &= (bool(np.isfinite(gm).all()) and r1 <= TOL
                    and np.array_equal(np.sort(got_idx), np.sort(idx)))
+        kb.moe_set_one_launch(0)
     finally:
         torch.cuda.synchronize()
         comm.close()

@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture
 def one_launch(lib):
     import kernels_b200 as kb
-    was = kb.moe_set_one_launch(True)
+    was = kb.moe_set_one_launch(3)   # the whole block and expert ranges
     yield kb
     kb.moe_set_one_launch(was)
 
