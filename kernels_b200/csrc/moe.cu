@@ -302,22 +302,56 @@ struct MoEMaps {
     int gu_segs, dn_segs;   // whole segments per row covered by gu5 / dn4 (0: maps unused)
 };
 
-// Stages `n` scale row blocks: block b is 16 rows of `srow` bytes at src(b),
-// landing as the aligned span at dst + b*sp.  Called by one whole warp: the
-// lanes size their blocks, lane 0 posts the total on `bar` (its one arrival),
-// then every lane issues its own copies.
-template <typename Src>
-__device__ __forceinline__ void stage_scale_blocks(uint32_t dst, int n, int sp, uint32_t srow,
-                                                   const uint8_t* end, uint32_t bar, int lane,
-                                                   Src src) {
-    uint32_t mine = 0;
-    for (int b = lane; b < n; b += 32) mine += span_copy(dst, src(b), 16 * srow, end).bytes;
+// A run of consecutive 16-row scale blocks of one expert, staged as one span
+// per scale array: entry G of row R of the run's i-th tile, array b, sits at
+// base + b*span + so[b] + (16*i + R)*srow + ES*G of the CTA's scale region.
+struct ScaleRun {
+    int base, span, first;   // region offset, bytes per array, the run's first item / tile
+    uint32_t so[4];          // where each array's rows start inside its span
+};
+constexpr int kRunsG = 3;    // experts one CTA's gate/up range may touch
+
+// Stages nr runs of A scale arrays each (A * nr <= 32) by one whole warp: one
+// bulk copy per (run, array) -- the rows of an expert's consecutive tiles are
+// contiguous, so a run costs A copies however many tiles it spans (a copy is
+// costed by the TMA unit per operation, not per byte).  Lane l takes array
+// l % A of run l / A; run_of(j, first, n) gives run j's first tile and tile
+// count, src_of(j, first, b) the start of its array b.  Lane 0 posts the bytes
+// on `bar` (its one arrival).
+template <typename RunOf, typename SrcOf>
+__device__ __forceinline__ void stage_scale_runs(int nr, int A, uint32_t srow, uint8_t* region,
+                                                 uint32_t bar, ScaleRun* runs, const uint8_t* end,
+                                                 int lane, RunOf&& run_of, SrcOf&& src_of) {
+    const int j = lane / A, b = lane - j * A;
+    const bool on = j < nr;
+    int ka = 0, n = 0, off = 0, span = 0;
+    if (on) {
+        for (int q = 0; q <= j; ++q) {   // this run's offset: the earlier runs' spans
+            int qa, qn;
+            run_of(q, qa, qn);
+            const int sq = (int)(((uint32_t)qn * kTileRows * srow + 32 + 15) & ~15u);
+            if (q < j) off += A * sq;
+            else { ka = qa; n = qn; span = sq; }
+        }
+    }
+    SpanCopy cp{nullptr, 0u, 0u};
+    if (on && n > 0) {
+        const uint8_t* src = src_of(j, ka, b);
+        cp = span_copy(smem_u32(region) + off + b * span, src, (uint32_t)n * kTileRows * srow, end);
+        runs[j].so[b] = (uint32_t)(uintptr_t)src & 15;
+        if (b == 0) {
+            runs[j].base = off;
+            runs[j].span = span;
+            runs[j].first = ka;
+        }
+    }
+    uint32_t total = cp.bytes;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
-    if (lane == 0) mbar_arrive_expect_tx(bar, mine);
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (lane == 0) mbar_arrive_expect_tx(bar, total);
     __syncwarp();
     fence_proxy_async_smem();
-    for (int b = lane; b < n; b += 32) bulk_copy(span_copy(dst + b * sp, src(b), 16 * srow, end), bar);
+    bulk_copy_hint(cp, bar, l2_evict_first());
 }
 
 // Pass 2.  A CTA owns a balanced range of items (selected expert, 16-row tile
@@ -368,19 +402,28 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_gate_up_mma(
         return tab->blob[s] + (proj ? a.off_up : a.off_gate) + (arr ? a.sub_b : a.sub_s) +
                (size_t)mt * kTileRows * srow;
     };
-    // item k: (slot position, tile, local expert, span offsets of its 4 scale blocks)
+    // item k: (slot position, tile, local expert, scale run)
+    const int s_first = i0 / mtiles;
     for (int k = threadIdx.x; k < nit; k += NW * 32) {
         const int it = i0 + k, s = it / mtiles, mt = it - s * mtiles;
-        int so = 0;
-        for (int b = 0; b < 4; ++b)
-            so |= (int)((uintptr_t)scale_src(s, mt, b >> 1, b & 1) & 15) << (4 * b);
-        itab[k] = make_int4(s, mt, tab->le[s], so);
+        itab[k] = make_int4(s, mt, tab->le[s], s - s_first);
     }
-    if (warp == 0 && nit > 0)
-        stage_scale_blocks(smem_u32(iscale), 4 * nit, sp, srow, a.pool_end, sbar, lane, [&](int b) {
-            const int it = i0 + (b >> 2), s = it / mtiles;
-            return scale_src(s, it - s * mtiles, (b >> 1) & 1, b & 1);
-        });
+    // the scales: per selected expert the items touch, 4 arrays, one copy each
+    __shared__ ScaleRun runs[kRunsG];
+    if (warp == 0 && nit > 0) {
+        const int i1 = i0 + nit - 1;
+        stage_scale_runs(
+            i1 / mtiles - s_first + 1, 4, srow, iscale, sbar, runs, a.pool_end, lane,
+            [&](int j, int& ka, int& n) {
+                const int s = s_first + j;
+                ka = max(i0, s * mtiles);
+                n = min(i1, s * mtiles + mtiles - 1) - ka + 1;
+            },
+            [&](int j, int ka, int b) {
+                const int s = s_first + j;
+                return scale_src(s, ka - s * mtiles, b >> 1, b & 1);
+            });
+    }
     __syncthreads();
 
     // unit u = warp + NW*i is (item u / upi, projection (u % upi) / parts, part u % parts)
@@ -430,17 +473,20 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_gate_up_mma(
     for (int i = 0; i < mine; ++i) {
         const int proj = cmp.r >= parts, part = cmp.r - proj * parts;
         const int c0 = part * PG::CHUNKS;
+        const ScaleRun& rn = runs[itab[cmp.k].w];
         ScaleView sv;
         sv.rs[0] = sv.rs[1] = srow;
-        const int so = itab[cmp.k].w >> (8 * proj);
-        sv.so[0] = (uint32_t)(so & 15) + 2 * (c0 / WPG);
-        sv.so[1] = (uint32_t)((so >> 4) & 15) + 2 * (c0 / WPG);
+#pragma unroll
+        for (int ar = 0; ar < 2; ++ar)
+            sv.so[ar] = rn.so[2 * proj + ar] + (uint32_t)(i0 + cmp.k - rn.first) * kTileRows * srow +
+                        2 * (c0 / WPG);
         if (live) live = wait_tile(bar_of(si), ph, &g_moe_err);
         float acc[2] = {0.f, 0.f};
         if (live)
-            tile_dot<LAYOUT, WPG>(code_of(si), iscale + (cmp.k * 2 + proj) * 2 * sp,
+            tile_dot<LAYOUT, WPG>(code_of(si), iscale + rn.base + 2 * proj * rn.span,
                                   xf + part * XWin<WPG>::STRIDE, gc + c0 / WPG,
-                                  min(PG::CHUNKS, nch - c0) / WPG, lane, lg, sv, (uint32_t)sp, acc);
+                                  min(PG::CHUNKS, nch - c0) / WPG, lane, lg, sv,
+                                  (uint32_t)rn.span, acc);
         const float v0 = quad_sum(acc[0]), v1 = quad_sum(acc[1]);
         if (t == 0) {
             const int row = cmp.k * kTileRows + lg.R;
@@ -524,9 +570,16 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
         return pd + (arr ? a.sub_b : a.sub_s) + (size_t)(T0 + k) * kTileRows * srow;
     };
 
+    // the scales of the CTA's tiles of its expert: one run, two copies
+    __shared__ ScaleRun run;
     if (act && warp == 0 && nt > 0)
-        stage_scale_blocks(smem_u32(tscale), 2 * nt, sp, srow, a.pool_end, sbar, lane,
-                           [&](int b) { return scale_src(b >> 1, b & 1); });
+        stage_scale_runs(
+            1, 2, srow, tscale, sbar, &run, a.pool_end, lane,
+            [&](int, int& ka, int& n) {
+                ka = 0;
+                n = nt;
+            },
+            [&](int, int ka, int b) { return scale_src(ka, b); });
 
     const int units = act ? nt * parts : 0;
     const int mine = units > warp ? (units - warp + NW - 1) / NW : 0;
@@ -586,13 +639,14 @@ __global__ void __launch_bounds__(NW * 32, 1) moe_down_mma(
         sv.rs[0] = sv.rs[1] = srow;
 #pragma unroll
         for (int ar = 0; ar < 2; ++ar)
-            sv.so[ar] = ((uint32_t)(uintptr_t)scale_src(cmp.k, ar) & 15) + 2 * (c0 / WPG);
+            sv.so[ar] = run.so[ar] + (uint32_t)cmp.k * kTileRows * srow + 2 * (c0 / WPG);
         if (live) live = wait_tile(bar_of(si), ph, &g_moe_err);
         float acc[2] = {0.f, 0.f};
         if (live)
-            tile_dot<LAYOUT, WPG>(code_of(si), tscale + cmp.k * 2 * sp,
+            tile_dot<LAYOUT, WPG>(code_of(si), tscale + run.base,
                                   xf + cmp.part * XWin<WPG>::STRIDE, gc + c0 / WPG,
-                                  min(PG::CHUNKS, nch - c0) / WPG, lane, lg, sv, (uint32_t)sp, acc);
+                                  min(PG::CHUNKS, nch - c0) / WPG, lane, lg, sv,
+                                  (uint32_t)run.span, acc);
         const float v0 = quad_sum(acc[0]), v1 = quad_sum(acc[1]);
         if (t == 0) {
             const int row = cmp.k * kTileRows + lg.R;
@@ -817,15 +871,6 @@ __host__ __device__ __forceinline__ int router_begin(int c, int G, int qW, int r
 // Start of CTA c's share of n units (c <= G; c * n < 2^31, checked on the host).
 __host__ __device__ __forceinline__ int share_begin(int c, int G, int n) { return c * n / G; }
 
-// A run of consecutive 16-row scale blocks of one expert, staged as one span
-// per scale array: entry G of row R of the run's i-th tile, array b, sits at
-// base + b*span + so[b] + (16*i + R)*srow + ES*G of the CTA's scale region.
-struct ScaleRun {
-    int base, span, first;   // region offset, bytes per array, the run's first item / tile
-    uint32_t so[4];          // where each array's rows start inside its span
-};
-constexpr int kRunsG = 3;    // experts one CTA's gate/up range may touch
-
 // A warp's position in its CTA's unit sequence (gate/up units, then down
 // units), decoded; advanced by NW units at a time with carries.
 struct FusedCursor {
@@ -1029,40 +1074,9 @@ __global__ void __launch_bounds__(kFusedWarps * 32, 1) moe_block_fused(
     // first, ahead of every code copy; down's at the end of the gate/up units.
     __shared__ ScaleRun runG[kRunsG], runD[kMaxTopK];
     const int p_first = k0 / mtiles;
-    // Lane l of the staging warp takes array l % A of run l / A: its span
-    // start is the sum of the earlier runs' spans (runs are few).
     auto stage_runs = [&](int nr, int A, uint32_t srow, uint8_t* region, uint32_t bar,
                           ScaleRun* runs, auto&& run_of, auto&& src_of) {
-        const int j = lane / A, b = lane - j * A;
-        const bool on = j < nr;
-        int ka = 0, n = 0, off = 0, span = 0;
-        if (on) {
-            for (int q = 0; q <= j; ++q) {
-                int qa, qn;
-                run_of(q, qa, qn);
-                const int sq = (int)(((uint32_t)qn * kTileRows * srow + 32 + 15) & ~15u);
-                if (q < j) off += A * sq; else { ka = qa; n = qn; span = sq; }
-            }
-        }
-        SpanCopy cp{nullptr, 0u, 0u};
-        if (on && n > 0) {
-            const uint8_t* src = src_of(j, ka, b);
-            cp = span_copy(smem_u32(region) + off + b * span, src, (uint32_t)n * kTileRows * srow,
-                           a.pool_end);
-            runs[j].so[b] = (uint32_t)(uintptr_t)src & 15;
-            if (b == 0) {
-                runs[j].base = off;
-                runs[j].span = span;
-                runs[j].first = ka;
-            }
-        }
-        uint32_t total = cp.bytes;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-        if (lane == 0) mbar_arrive_expect_tx(bar, total);
-        __syncwarp();
-        fence_proxy_async_smem();
-        bulk_copy_hint(cp, bar, l2_evict_first());
+        stage_scale_runs(nr, A, srow, region, bar, runs, a.pool_end, lane, run_of, src_of);
     };
     if (warp == 0 && nitems > 0) {
         const int k1 = k0 + nitems - 1;
@@ -1838,9 +1852,10 @@ int launch_gate_up(const MoEArgs& a, const uint32_t* idx, const uint32_t* local,
         const int items = a.top_k * (a.inter / kTileRows);
         const int grid = std::max(1, std::min(di.sm_count, items));
         const int items_max = (items + grid - 1) / grid;
-        if (gate_up_mma_smem(a, 16, items_max) <= di.max_smem_optin)
+        // (a CTA's items then touch at most two experts: its scale runs)
+        if (items_max <= a.inter / kTileRows && gate_up_mma_smem(a, 16, items_max) <= di.max_smem_optin)
             return gate_up_mma<LAYOUT, 16>(mp, a, idx, local, xh, h, xsh, grid, items_max, st);
-        if (gate_up_mma_smem(a, 8, items_max) <= di.max_smem_optin)
+        if (items_max <= a.inter / kTileRows && gate_up_mma_smem(a, 8, items_max) <= di.max_smem_optin)
             return gate_up_mma<LAYOUT, 8>(mp, a, idx, local, xh, h, xsh, grid, items_max, st);
     }
     const int smem = a.hidden * 2 + (a.hidden / 32) * 8;
