@@ -343,6 +343,12 @@ int graft_moe_block_ex(const void* pool, const void* R, const void* x, void* y,
  * default is 0 (three launches) unless set.  Returns the previous setting.
  * Process-wide, not thread-safe against concurrent block calls. */
 int graft_moe_set_one_launch(int on);
+/* The three-launch block's down + combine pass: split = 1 runs it on every SM
+ * without thread-block clusters, its units split evenly and a tile split
+ * between CTAs handed on through the scratch's `sync` region; split = 0 (the
+ * default, measured faster) runs it as clusters of top_k CTAs combining
+ * through distributed shared memory.  Returns the previous setting. */
+int graft_moe_set_down_pass(int split);
 
 /* graft_moe_block_ex without a caller-provided scratch buffer -- for callers
  * that cannot call cudaMalloc (hosts that own all device memory through their

@@ -311,6 +311,12 @@ def gemm_set_tcgen05(on: bool) -> bool:
     return bool(load().graft_gemm_set_tcgen05(1 if on else 0))
 
 
+def moe_set_down_pass(split: bool) -> bool:
+    """The block's down pass on every SM without clusters (True) or as
+    clusters of top_k CTAs (False, the default); returns the previous setting."""
+    return bool(load().graft_moe_set_down_pass(1 if split else 0))
+
+
 def moe_set_one_launch(on) -> int:
     """Where the MoE block runs as one launch instead of three: True/1 the
     whole block on one GPU, 2 a rank's share of an expert-parallel block, 3

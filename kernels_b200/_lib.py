@@ -113,6 +113,7 @@ SIGNATURES: dict[str, tuple] = {
     "graft_moe_scratch_bytes": (SIZE, [C.POINTER(MoEParams)]),
     "graft_moe_scratch_carve": (INT, [P, SIZE, C.POINTER(MoEParams), C.POINTER(MoEScratch)]),
     "graft_moe_set_one_launch": (INT, [INT]),
+    "graft_moe_set_down_pass": (INT, [INT]),
     "graft_gemm_set_tcgen05": (INT, [INT]),
     "graft_moe_scratch_init": (INT, [C.POINTER(MoEParams), C.POINTER(MoEScratch), P]),
     "graft_moe_block": (INT, [P, P, P, P, C.POINTER(MoEParams), C.POINTER(MoEScratch), P]),

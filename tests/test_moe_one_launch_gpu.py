@@ -143,3 +143,28 @@ def test_one_launch_expert_ranges_sum_to_block(one_launch):
         assert norm_rel(got, part) <= TOL if np.any(part) else not np.any(got)
         total += got
     assert norm_rel(total, oracle_block(P, pool, R, x)[4]) <= TOL
+
+
+def test_cluster_free_down_pass_matches_clusters(lib):
+    """graft_moe_set_down_pass(1): the down + combine pass without clusters gives
+    the cluster pass's bits (same sums, same order) on config 3, call after call."""
+    import torch
+    import kernels_b200 as kb
+    from kernels_b200 import synth
+    P, pool, R, _ = baseline_block(kb, seed=8)
+    ws = kb.MoEWorkspace(P)
+    y = torch.empty(P.hidden, dtype=torch.float16, device="cuda")
+    was = kb.moe_set_down_pass(False)
+    try:
+        for s in range(3):
+            x = synth.activations(P.hidden, seed=30 + s)
+            outs = []
+            for split in (False, True):
+                kb.moe_set_down_pass(split)
+                y.fill_(float("nan"))
+                kb.moe_block_ex(pool, R, x, y, P, fmt16(kb, P), ws)
+                outs.append(host(y).copy())
+            assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16)), s
+        assert kb.device_errors(clear=True)["moe"] == 0
+    finally:
+        kb.moe_set_down_pass(was)
