@@ -4,9 +4,9 @@ the counterpart of the reference harness binaries' flags (int4gemv --M --K --G
 
     python -m kernels_b200.run int4 --M 128256 --K 4096 [--G 64] [--iters 5] [--copies 2]
     python -m kernels_b200.run vq --M 14336 --K 4096 [--s32]
-    python -m kernels_b200.run moe [--experts 128] [--top-k 4]
+    python -m kernels_b200.run moe [--experts 128] [--top-k 4] [--one-launch 1]
     python -m kernels_b200.run stream --mbytes 1024
-    python -m kernels_b200.run batch --M 128256 --K 4096 --B 8
+    python -m kernels_b200.run batch --M 128256 --K 4096 --B 8 [--tcgen05]
     python -m kernels_b200.run vqquant --M 4096 --K 4096
     python -m kernels_b200.run expert [--copies 4]     # one gpt-oss expert (bf16 format)
 
@@ -34,6 +34,10 @@ def main() -> None:
     ap.add_argument("--B", type=int, default=8, help="batch: tokens per call")
     ap.add_argument("--f32out", action="store_true")
     ap.add_argument("--s32", action="store_true", help="vq: per-32 scales (the reference's form)")
+    ap.add_argument("--tcgen05", action="store_true",
+                    help="batch: 9..16 tokens on the tcgen05 kernel (graft_gemm_set_tcgen05)")
+    ap.add_argument("--one-launch", type=int, default=0,
+                    help="moe: graft_moe_set_one_launch bits (1: the whole block in one launch)")
     a = ap.parse_args()
 
     import torch
@@ -66,6 +70,7 @@ def main() -> None:
         f = lambda i: kb.gemv_vq_ex(ws[i % a.copies]["IDX"], ws[i % a.copies]["C"],  # noqa
                                     ws[i % a.copies]["S"], sg, x, y, P)
     elif a.kernel == "batch":
+        kb.gemm_set_tcgen05(a.tcgen05)
         ws = [synth.int4_weights(a.M, a.K, a.G, seed=c) for c in range(a.copies)]
         X = torch.stack([synth.activations(a.K, seed=50 + b) for b in range(a.B)])
         Y = torch.empty((a.B, a.M), dtype=torch.float16, device="cuda")
@@ -89,6 +94,7 @@ def main() -> None:
         nbytes = P.blob
         f = lambda i: kb.expert_forward(pool[(i % a.copies) * P.blob:], x, y, P, scratch)  # noqa
     elif a.kernel == "moe":
+        kb.moe_set_one_launch(a.one_launch)
         P = kb.moe_params(2880, 2880, a.experts, a.top_k)
         pool, R = synth.moe_pool(P, scale_f16=True, has_bias_out=False, act_f16=True)
         xs_ = [synth.activations(2880, seed=s) for s in range(8)]
