@@ -11,7 +11,10 @@ the counterpart of the reference harness binaries' flags (int4gemv --M --K --G
     python -m kernels_b200.run expert [--copies 4]     # one gpt-oss expert (bf16 format)
 
 Each iteration is one launch on a rotating weight copy, timed with CUDA events;
-use it for small profiler captures (a few launches, a few GB).
+use it for small profiler captures (a few launches, a few GB).  --graph N
+instead times N launches (copies rotating) captured in one CUDA graph and
+replayed back to back, as the bench times its steps, and reports the mean
+time per launch (the launch overhead of a lone call excluded).
 """
 from __future__ import annotations
 
@@ -38,6 +41,8 @@ def main() -> None:
                     help="batch: 9..16 tokens on the tcgen05 kernel (graft_gemm_set_tcgen05)")
     ap.add_argument("--one-launch", type=int, default=0,
                     help="moe: graft_moe_set_one_launch bits (1: the whole block in one launch)")
+    ap.add_argument("--graph", type=int, default=0,
+                    help="time N launches captured in one CUDA graph (mean per launch)")
     a = ap.parse_args()
 
     import torch
@@ -123,9 +128,32 @@ def main() -> None:
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1) * 1e3)
     best = min(times)
-    print(json.dumps({"kernel": a.kernel, "M": a.M, "K": a.K, "best_us": round(best, 3),
-                      "gbs": round(nbytes / best / 1e3, 1), "bytes": nbytes,
-                      "times_us": [round(t, 2) for t in times]}))
+    out = {"kernel": a.kernel, "M": a.M, "K": a.K, "best_us": round(best, 3),
+           "gbs": round(nbytes / best / 1e3, 1), "bytes": nbytes,
+           "times_us": [round(t, 2) for t in times]}
+    if a.graph > 0:
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(a.graph):
+                f(i)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        reps = []
+        for _ in range(max(a.iters, 1)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            reps.append(e0.elapsed_time(e1) * 1e3 / a.graph)
+        per = sorted(reps)[len(reps) // 2]
+        out.update({"graph_launches": a.graph, "graph_us_per_launch": round(per, 3),
+                    "graph_gbs": round(nbytes / per / 1e3, 1)})
+        del g
+    print(json.dumps(out))
 
 
 if __name__ == "__main__":

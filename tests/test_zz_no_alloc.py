@@ -3,8 +3,9 @@ cudaMalloc (hosts that own all device memory and give a library no allocator,
 hosts that must not allocate after start-up).  It keeps its scratch in a fixed
 array inside the library; these
 tests call it through the C ABI and check it against graft_moe_block_ex with a
-caller-provided workspace, twice in a row with different tokens, so that the
-second call cannot pass on the first call's leftovers.
+caller-provided workspace and against the fp64 oracle, twice in a row with
+different tokens, so that the second call cannot pass on the first call's
+leftovers.
 
 This file is collected last on purpose: it must pass both alone in a fresh
 process and after every other test has used the library."""
@@ -16,6 +17,7 @@ import numpy as np
 import pytest
 
 from conftest import TOL, norm_rel
+from test_moe_gpu import oracle_block
 
 pytestmark = pytest.mark.gpu
 
@@ -55,6 +57,10 @@ def test_noalloc_matches_workspace_twice_in_a_row(lib, hidden, inter, n_experts,
         assert np.isfinite(got).all()
         assert norm_rel(got, ref) <= TOL
     assert norm_rel(outs[0].cpu().numpy(), outs[1].cpu().numpy()) > 0   # different tokens
+    # and each no-allocation output against the fp64 oracle of the block itself
+    for x, y in zip(xs, outs):
+        yref = oracle_block(P, pool, R, x)[4]
+        assert norm_rel(y.cpu().numpy(), yref) <= TOL
 
 
 def test_noalloc_rejects_configurations_beyond_its_scratch(lib):
