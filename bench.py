@@ -541,7 +541,9 @@ def main() -> None:
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                 "traffic": traffic, "peak_source": peaks["source"],
-                "kernel": "int4_gemv_kernel (graft_gemv_int4_sb_f16out; tensor-pipe tile engine)",
+                "kernel": ("graft_gemv_int4_sb_f16out on the tensor-pipe tile engine: "
+                           "int4_gemv_kernel for the mid shapes, int4_gemm_batch_kernel's "
+                           "one-token mode for the lm_head"),
                 "bytes_per_launch": bytes_step // len(SWEEP)}
 
     detail = {}
