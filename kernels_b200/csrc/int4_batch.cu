@@ -605,6 +605,20 @@ int int4_gemm_batch(const void* W, const void* SB, const void* X, void* Y, long 
     return GRAFT_OK;
 }
 
+// Error bits of the batched kernel (a bounded wait that gave up).
+unsigned int4_batch_device_errors(bool clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_batch_err, sizeof v) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (clear && v) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_batch_err, &z, sizeof z);
+    }
+    return v;
+}
+
 template <int WPG>
 bool batch1_fits(const GraftGemvParams* P, const DeviceInfo& di) {
     using PG = PartGeom<WPG>;

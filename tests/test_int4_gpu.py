@@ -113,6 +113,28 @@ def test_config4_lmhead_full_shape(lib, B):
         assert elem_rel(got[b], ref) <= TOL_ELEM, b
 
 
+@pytest.mark.parametrize("M,K,G", [(20000, 4096, 32), (9000, 14336, 64), (60013, 4096, 128),
+                                   (60001, 2048, 64)])
+def test_tall_shapes_one_token_mode(lib, M, K, G):
+    """Tall matrices whose scale rows are 16-byte strided and which give at
+    least 6 units (16-row tile x K-part) per warp on 148 SMs run the batched
+    kernel's one-token mode rather than the batch-1 tile GEMV: every group size
+    it takes, long rows, and row counts that end in a partial 16-row tile."""
+    import torch
+    import kernels_b200 as kb
+    w, x = baseline_case(kb, M, K, G=G, seed=M % 97)
+    P = kb.gemv_params(M, K, G)
+    y = torch.full((M,), float("nan"), dtype=torch.float16, device="cuda")
+    kb.gemv_int4_sb_f16out(w["W"], w["SB"], x, y, P)
+    got = host(y).astype(np.float32)
+    ref = oracle.gemv_int4_sb(host(w["W"]).view(np.uint32), host(w["SB"]).view(np.uint16),
+                              host(x).view(np.uint16), G)
+    assert np.isfinite(got).all()
+    assert norm_rel(got, ref) <= TOL
+    assert elem_rel(got, ref) <= TOL_ELEM
+    assert kb.device_errors(clear=True)["int4"] == 0
+
+
 @pytest.mark.parametrize("M,K,G", [(1, 32, 32), (7, 64, 32), (33, 96, 96), (130, 2880, 64),
                                    (257, 512, 128), (61, 1024, 256), (9, 65536, 64),
                                    (5000, 160, 32)])
