@@ -92,23 +92,31 @@ struct GemvArgs {
     const P2PGather* gather;   // fused all-gather of y (fp16), or null
     long y_off;                // element offset of this rank's rows in the gathered y
     int map3;                  // wmap is 3-D (K % 256 == 0): one copy per unit, not one per segment
+    int qcells;                // cells per (row, part, lane of the quad): no shuffles per unit
     const float* x32;          // fp32 activations (rounded to fp16 when staged), or null
     const uint16_t* BI;        // bf16 per-row output bias added to y, or null
 };
+
+// Row i's total from its cells: parts x lanes values (lanes 4: one per lane
+// of the row's quad, else 1: the quad's sum) at row stride rs floats, added
+// in (part, lane) order.
+__device__ __forceinline__ float row_total(const float* cells, int parts, int lanes, int rs,
+                                           int i) {
+    float v = 0.f;
+    const float* c = cells + i * rs;
+    for (int q = 0; q < parts * lanes; ++q) v += c[q];
+    return v;
+}
 
 // Fused all-gather epilogue: rows [r0, r1) (part sums in `cells`) as fp16 in
 // smem `ybuf`, then into every rank's copy of the symmetric output (this
 // rank's block at element y_off), and the peers' rows of the same range into
 // this rank's copy (graft_p2p.cuh).
 __device__ __forceinline__ void gather_rows(const P2PGather* g, const float* cells, int parts,
-                                            int r0, int r1, long y_off, long M, uint32_t E,
-                                            __half* ybuf, int nthreads) {
+                                            int lanes, int rs, int r0, int r1, long y_off, long M,
+                                            uint32_t E, __half* ybuf, int nthreads) {
     const int n = r1 - r0;
-    for (int i = threadIdx.x; i < n; i += nthreads) {
-        float v = 0.f;
-        for (int q = 0; q < parts; ++q) v += cells[i * parts + q];
-        ybuf[i] = __float2half_rn(v);
-    }
+    for (int i = threadIdx.x; i < n; i += nthreads) ybuf[i] = __float2half_rn(row_total(cells, parts, lanes, rs, i));
     __syncthreads();
     gather_rows_ll(g, E, ybuf, n, false, n, 1, 0, y_off - g->rank * M, M, r0);
     fused_close(g, E);
@@ -117,10 +125,17 @@ __device__ __forceinline__ void gather_rows(const P2PGather* g, const float* cel
 // Shared memory: barriers, then (1024-aligned) the code ring, the scale
 // ring, x fragments, zero fragments, group constants and (row, part) cells.
 constexpr int kHeadBytes = 256;
+// Floats per row of cells: one per part, or (qcells) one per part and lane of
+// the row's quad, at an odd multiple of 4 so that a warp's 32 stores (8 rows
+// x 4 lanes) fall on 32 banks.
+__host__ __device__ inline int cell_stride(int parts, int qcells) {
+    return qcells ? 4 * (parts | 1) : parts;
+}
+
 template <int WPG>
-__host__ __device__ inline int smem_after_rings(int K, int rows_max, int parts) {
-    return XWin<WPG>::uint4s(K) * 16 + ((K / (32 * WPG) + 9) & ~1) * 8 + rows_max * parts * 4 +
-           ((rows_max * 2 + 15) & ~15);
+__host__ __device__ inline int smem_after_rings(int K, int rows_max, int parts, int qcells) {
+    return XWin<WPG>::uint4s(K) * 16 + ((K / (32 * WPG) + 9) & ~1) * 8 +
+           rows_max * cell_stride(parts, qcells) * 4 + ((rows_max * 2 + 15) & ~15);
 }
 
 template <int LAYOUT, bool F16OUT, int WPG, int NW>
@@ -138,6 +153,7 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
     float2* gc = reinterpret_cast<float2*>(xf + XWin<WPG>::uint4s(a.K));
     // (group constants padded to an even count: cells and the fp16 staging stay 16-byte aligned)
     float* cells = reinterpret_cast<float*>(gc + ((a.K / (32 * WPG) + 9) & ~1));
+    const int clanes = a.qcells ? 4 : 1, crs = cell_stride(a.parts, a.qcells);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles = (a.M + kTileRows - 1) / kTileRows;
@@ -256,11 +272,19 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
         if (live)
             tile_dot<LAYOUT, WPG>(code_of(si), scale_of(si), xf + cmp.part * XWin<WPG>::STRIDE,
                                   gc + c0 / WPG, nc / WPG, lane, lg, sv, (uint32_t)a.scap, acc);
-        const float v0 = quad_sum(acc[0]), v1 = quad_sum(acc[1]);
-        if (t == 0) {
-            const int lrow = kTileRows * cmp.tile + lg.R;   // CTA-local rows R and R+8
-            if (r0 + lrow < r1) cells[lrow * a.parts + cmp.part] = v0;
-            if (r0 + lrow + 8 < r1) cells[(lrow + 8) * a.parts + cmp.part] = v1;
+        const int lrow = kTileRows * cmp.tile + lg.R;   // CTA-local rows R and R+8
+        if (a.qcells) {
+            // each lane's share, no shuffle: cell (row, part, t) at row stride
+            // crs, which puts the 32 lanes' stores on 32 banks
+            float* c = cells + lrow * crs + 4 * cmp.part + t;
+            if (r0 + lrow < r1) c[0] = acc[0];
+            if (r0 + lrow + 8 < r1) c[8 * crs] = acc[1];
+        } else {
+            const float v0 = quad_sum(acc[0]), v1 = quad_sum(acc[1]);
+            if (t == 0) {
+                if (r0 + lrow < r1) cells[lrow * crs + cmp.part] = v0;
+                if (r0 + lrow + 8 < r1) cells[(lrow + 8) * crs + cmp.part] = v1;
+            }
         }
         __syncwarp();
         if (live && i + kDepth < mine) {
@@ -272,13 +296,12 @@ __global__ void __launch_bounds__(NW * 32, 1) int4_gemv_kernel(const __grid_cons
     }
     __syncthreads();
     if (F16OUT && a.gather) {
-        gather_rows(a.gather, cells, a.parts, r0, r1, a.y_off, a.M, E,
-                    reinterpret_cast<__half*>(cells + kTileRows * (T1 - T0) * a.parts), NW * 32);
+        gather_rows(a.gather, cells, a.parts, clanes, crs, r0, r1, a.y_off, a.M, E,
+                    reinterpret_cast<__half*>(cells + kTileRows * (T1 - T0) * crs), NW * 32);
         return;
     }
     for (int i = threadIdx.x; i < r1 - r0; i += NW * 32) {
-        float v = 0.f;
-        for (int q = 0; q < a.parts; ++q) v += cells[i * a.parts + q];
+        float v = row_total(cells, a.parts, clanes, crs, i);
         if (a.BI) v += bf2f(a.BI[r0 + i]);
         if (F16OUT) reinterpret_cast<__half*>(a.y)[r0 + i] = __float2half_rn(v);
         else reinterpret_cast<float*>(a.y)[r0 + i] = v;
@@ -453,8 +476,13 @@ int launch_tiles(GemvArgs a, const DeviceInfo& di, cudaStream_t st, bool* fits) 
     }
     auto smem_of = [&](int nw) {
         return kHeadBytes + 1024 + nw * kDepth * (PG::CODE_BYTES + SG::NARR * a.scap) +
-               smem_after_rings<WPG>(a.K, rows_max, a.parts);
+               smem_after_rings<WPG>(a.K, rows_max, a.parts, a.qcells);
     };
+    // per-lane cells where they fit beside 16 warps' rings: no quad shuffle on
+    // every unit's dependent path (measured on B200: 65536x4096 fp32 y 27.96 ->
+    // 27.48 us, 6144x4096 -0.1 us, the other config-1 shapes level)
+    a.qcells = 1;
+    if (smem_of(16) > di.max_smem_optin) a.qcells = 0;
     // 16 warps where the rings fit, else 8
     const int nw = smem_of(16) <= di.max_smem_optin ? 16 : 8;
     if (smem_of(nw) > di.max_smem_optin) return GRAFT_OK;
