@@ -726,12 +726,15 @@ def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status,
     fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=True,
                         n_experts=128)
     ep = {}
-    # the NCCL form (ncclAllReduce of the fp32 partials) beside the default, and
-    # the one-launch block with the fused reduction
+    # the NCCL form (ncclAllReduce of the fp32 partials) beside the default, the
+    # one-launch block with the fused reduction, and the three launches with the
+    # cluster-free down pass
     was_one = kb.moe_set_one_launch(0)
-    for form in (["fused", "one_launch", "nccl"] if comm.fused else ["nccl"]):
+    was_split = kb.moe_set_down_pass(False)
+    for form in (["fused", "one_launch", "split_down", "nccl"] if comm.fused else ["nccl"]):
         comm.set_fused(form != "nccl")
         kb.moe_set_one_launch(2 if form == "one_launch" else 0)
+        kb.moe_set_down_pass(form == "split_down")
         torch.cuda.synchronize()
         barrier()
         t = Timer(torch, lambda i: kb.moe_block_ep(comm, shard, R, xs_[i % 16], y, Pm, fmt, wsp),
@@ -746,8 +749,10 @@ def measure_multi(torch, kb, synth, comm, dist, world, rank, barrier, status,
         barrier()
     comm.set_fused(True)
     kb.moe_set_one_launch(was_one)
+    kb.moe_set_down_pass(was_split)
     d["moe_config3_ep"] = {"us_per_token": ep.get("fused", ep["nccl"]),
                            "one_launch_us_per_token": ep.get("one_launch"),
+                           "split_down_us_per_token": ep.get("split_down"),
                            "nccl_us_per_token": ep["nccl"],
                            "reduce": ("fused into the down pass over peer memory" if "fused" in ep
                                       else "ncclAllReduce"),

@@ -117,10 +117,15 @@ def main() -> int:
         ws = kb.MoEWorkspace(P)
         # three tokens back to back (the reduce slots and counts are reused call after
         # call), fp32 y, then one with fp16 y (the epilogue's conversion branch); as
-        # three launches, then as one launch per rank (the one-launch block)
-        for it, (y_f16, one) in enumerate([(False, 0), (False, 0), (False, 0), (True, 0),
-                                           (False, 2), (False, 2), (True, 2)]):
+        # three launches, as one launch per rank (the one-launch block), and as three
+        # launches with the cluster-free down pass (split tiles handed on, a rank
+        # without a selected expert sending zero rows)
+        for it, (y_f16, one, split) in enumerate([
+                (False, 0, 0), (False, 0, 0), (False, 0, 0), (True, 0, 0),
+                (False, 2, 0), (False, 2, 0), (True, 2, 0),
+                (False, 0, 1), (False, 0, 1), (True, 0, 1)]):
             kb.moe_set_one_launch(one)
+            kb.moe_set_down_pass(bool(split))
             xm = synth.activations(2880, seed=14 + it)
             fmt = kb.moe_format(scale_f16=True, has_bias_out=False, act_f16=True, y_f16=y_f16,
                                 n_experts=P.n_experts)
@@ -134,13 +139,15 @@ def main() -> int:
             gm = ym.float().cpu().numpy()
             r1, r2 = rels(gm, yref)
             print(f"rank {rank}: ep moe token {it} ({'f16' if y_f16 else 'f32'} y, "
-                  f"{'one launch' if one else 'three launches'}) "
+                  f"{'one launch' if one else 'three launches'}"
+                  f"{', cluster-free down' if split else ''}) "
                   f"max|d|/max|ref| = {r1:.2e} elem {r2:.2e} top-k {list(got_idx)}", flush=True)
             # max-norm for the block, as the reference checks it (moe-fused/src/main.mm:336-376):
             # h is fp16 in the kernels, as in the reference's, and fp64 in the oracle
             ok &= (bool(np.isfinite(gm).all()) and r1 <= TOL
                    and np.array_equal(np.sort(got_idx), np.sort(idx)))
         kb.moe_set_one_launch(0)
+        kb.moe_set_down_pass(False)
     finally:
         torch.cuda.synchronize()
         comm.close()
