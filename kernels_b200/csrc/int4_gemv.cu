@@ -3,12 +3,16 @@
 //
 // The GEMV is a persistent grid over the tensor-pipe row-dot engine of
 // q4_mma.cuh.  Each CTA owns a contiguous, balanced range of 16-row tiles; a
-// unit is one tile x one K-part (1024 weights), and the CTA's units are dealt
-// to its eight warps round-robin.  Each unit's row sums go to a per-(row, part)
-// shared-memory cell, added in part order at the end, so results do not
-// depend on timing.  Shapes the engine does not cover (group sizes other than
-// 32/64/128, rows too long for shared memory) use the register-direct engine
-// of q4_rows.cuh.
+// unit is one tile x one K-part (a window of 8 groups), and the CTA's units
+// are dealt to its 16 (or 8) warps round-robin.  Each lane stores its share of
+// a unit's row sums in a (row, part, lane-of-quad) shared-memory cell (or,
+// where those do not fit, the quad's sum in a (row, part) cell); the cells
+// are added in a fixed order at the end, so results do not depend on timing.
+// Shapes the engine does not cover (group sizes other than 32/64/128, rows too
+// long for shared memory) use the register-direct engine of q4_rows.cuh.  The
+// fp16-output entry point sends tall matrices (>= 6 units per warp) and scale
+// rows that are not 16-byte strided to the batched kernel's one-token mode
+// (int4_batch.cu).
 //
 // Launch: programmatic dependent launch, so the weight stream of a GEMV starts
 // while the previous kernel on the stream is still draining (set
@@ -116,7 +120,8 @@ __device__ __forceinline__ void gather_rows(const P2PGather* g, const float* cel
                                             int lanes, int rs, int r0, int r1, long y_off, long M,
                                             uint32_t E, __half* ybuf, int nthreads) {
     const int n = r1 - r0;
-    for (int i = threadIdx.x; i < n; i += nthreads) ybuf[i] = __float2half_rn(row_total(cells, parts, lanes, rs, i));
+    for (int i = threadIdx.x; i < n; i += nthreads)
+        ybuf[i] = __float2half_rn(row_total(cells, parts, lanes, rs, i));
     __syncthreads();
     gather_rows_ll(g, E, ybuf, n, false, n, 1, 0, y_off - g->rank * M, M, r0);
     fused_close(g, E);
