@@ -61,6 +61,8 @@ def test_noalloc_matches_workspace_twice_in_a_row(lib, hidden, inter, n_experts,
     for x, y in zip(xs, outs):
         yref = oracle_block(P, pool, R, x)[4]
         assert norm_rel(y.cpu().numpy(), yref) <= TOL
+    # no bounded wait of the block's kernels gave up
+    assert kb.device_errors(clear=True)["moe"] == 0
 
 
 def test_noalloc_rejects_configurations_beyond_its_scratch(lib):
